@@ -1,0 +1,318 @@
+"""Benchmark of the hot path: the tropical binary contraction.
+
+Workload (the config the target is quoted on):
+MaxPlus<f32> 'ij,jk->ik' with i = j = k = 2048, argmax tracking on, inputs f32
+U[-1,1) from the shared seeded generator.  One step = one
+om_b200_contract call (the reference's Backend::contract_with_argmax).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Prints ONE JSON line (rank 0).  `value` is device-timed throughput with the
+inputs resident in HBM (CUDA events on the backend's stream, L2 flushed by a
+256 MiB write before every timed step); `e2e` is the same call made from
+pinned host buffers with the host->device copies of A and B and the
+device->host copies of C and argmax inside the timed region.  With N > 1 every
+rank runs an independent replica (the binary contraction does not shard);
+`value` is the sum over ranks using the max over ranks of the time.
+`--impl reference` times the CPU restatement of the reference's
+generic_gemm_with_argmax (oracle/) on all host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+M = N = K = 2048
+SEED = 0x5EED
+OPS = 2.0 * M * N * K  # one (x) and one (+) per (i, j, k)
+METRIC = "tropical semiring GOP/s (binary contract)"
+UNIT = "GOP/s"
+WORKLOAD = "maxplus_f32_ij_jk_ik_2048x2048x2048_argmax"
+# FP32 CUDA-core peak (no measured figure exists for it in MEASURED_PEAKS.json):
+# 148 SMs x 128 lanes x 2 ops x 1965 MHz (max SM clock).
+FP32_PEAK_TOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
+# kernel, from the ncu capture summarised in profiles/ (None until captured).
+NCU_TRAFFIC_BYTES = None
+
+
+def load_pkg():
+    import importlib.util
+    d = os.path.join(ROOT, "omeinsum-rs_b200")
+    if "omeinsum_b200" in sys.modules:
+        return sys.modules["omeinsum_b200"]
+    spec = importlib.util.spec_from_file_location("omeinsum_b200", os.path.join(d, "__init__.py"),
+                                                  submodule_search_locations=[d])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["omeinsum_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def inputs():
+    import oracle as orc
+    return orc.uniform(SEED, M * K), orc.uniform(SEED + 1, K * N)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.proc = gpu, None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample(threads: int, rows: int):
+    """Times the restated reference loop (generic_gemm_with_argmax) on the
+    first `rows` rows of the workload (all columns, full k)."""
+    import oracle as orc
+    a, b = inputs()
+    sub = np.ascontiguousarray(a.reshape(K, M)[:, :rows]).reshape(-1)
+    t0 = time.perf_counter()
+    orc.gemm("maxplus", sub, b, rows, K, N, argmax=True, threads=threads)
+    dt = time.perf_counter() - t0
+    return 2.0 * rows * N * K / dt / 1e9, dt
+
+
+def run_reference(args, rank, world):
+    import oracle as orc
+    if rank != 0:
+        return
+    threads = orc.max_threads()
+    rows = max(8, min(M, int(os.environ.get("OM_BENCH_REF_ROWS", "64"))))
+    for _ in range(args.warmup):
+        cpu_sample(threads, max(8, rows // 8))
+    vals, total = [], 0.0
+    for _ in range(args.steps):
+        v, dt = cpu_sample(threads, rows)
+        vals.append(v)
+        total += dt
+    value = statistics.median(vals)
+    sample = (f"rows 0..{rows - 1} of the {M}x{N}x{K} workload per step (all columns, full k), "
+              f"oracle/ restatement of generic_gemm_with_argmax, OpenMP over columns")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded U[-1,1))",
+        "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "algebra": "MaxPlus<f32>",
+                   "argmax": True},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+    om = load_pkg()
+    torch.cuda.set_device(local_rank)
+    be = om.B200(local_rank)
+    a, b = inputs()
+    A, B = be.from_slice(a), be.from_slice(b)
+    C = be.alloc(M * N, np.float32)
+    AM = be.alloc(M * N, np.uint32)
+    stream = torch.cuda.ExternalStream(be.stream(), device=local_rank)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local_rank}")
+
+    def step():
+        be.contract_into("maxplus", A, [M, K], [1, M], [0, 1], B, [K, N], [1, K], [1, 2],
+                         [M, N], [0, 2], C, AM)
+
+    for _ in range(args.warmup):
+        step()
+    be.synchronize()
+
+    # correctness guard on the benchmarked output (sampled rows vs the oracle)
+    if rank == 0 and not args.no_check:
+        import oracle as orc
+        rows = [0, 777, 2047]
+        cv, av = C.to_vec().reshape(N, M), AM.to_vec().reshape(N, M)
+        sub = np.ascontiguousarray(a.reshape(K, M)[:, rows]).reshape(-1)
+        rc, ram = orc.gemm("maxplus", sub, b, len(rows), K, N, argmax=True,
+                           threads=orc.max_threads())
+        assert np.array_equal(cv[:, rows].reshape(-1).view(np.uint32),
+                              rc.reshape(N, len(rows)).reshape(-1).view(np.uint32)), "bench check"
+        assert np.array_equal(av[:, rows].reshape(-1), ram.reshape(N, len(rows)).reshape(-1))
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        be.synchronize()
+
+    # ---- device-timed region: inputs resident in HBM ----------------------
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    om.launch_count()
+    be.profile(True)
+    barrier()
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.fill_(i & 0xFF)  # L2 flush, outside the events
+                ev[i][0].record(stream)
+            step()
+            with torch.cuda.stream(stream):
+                ev[i][1].record(stream)
+        barrier()
+    launches = om.launch_count()
+    prof = be.profile_report()
+    be.profile(False)
+    step_ms = [s.elapsed_time(e) for s, e in ev]
+    total_ms = sum(step_ms)
+    t_local = torch.tensor([total_ms], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if world > 1:
+        torch.distributed.all_reduce(t_local, op=torch.distributed.ReduceOp.MAX)
+    t_max = float(t_local.item())
+    value = world * args.steps * OPS / (t_max / 1e3) / 1e9
+
+    # ---- end-to-end: pinned host buffers through the C ABI ------------------
+    ha = torch.from_numpy(a).pin_memory()
+    hb = torch.from_numpy(b).pin_memory()
+    hc = torch.empty(M * N, dtype=torch.float32).pin_memory()
+    hm = torch.empty(M * N, dtype=torch.int32).pin_memory()
+    L = om.lib()
+
+    def e2e_step():
+        om._check(L.om_b200_upload(be.h, A.ptr, ha.data_ptr(), A.nbytes))
+        om._check(L.om_b200_upload(be.h, B.ptr, hb.data_ptr(), B.nbytes))
+        step()
+        om._check(L.om_b200_download(be.h, hc.data_ptr(), C.ptr, C.nbytes))
+        om._check(L.om_b200_download(be.h, hm.data_ptr(), AM.ptr, AM.nbytes))
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    t_e2e = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if world > 1:
+        torch.distributed.all_reduce(t_e2e, op=torch.distributed.ReduceOp.MAX)
+    e2e_value = world * args.steps * OPS / float(t_e2e.item()) / 1e9
+
+    if rank != 0:
+        return
+    # roofline of the dominant kernel (device time per launch from the events)
+    top = max(prof.items(), key=lambda kv: kv[1][0]) if prof else ("?", (0.0, 1))
+    kname, (kms, kn) = top
+    achieved = OPS / (kms / kn / 1e3) / 1e12 if kn and kms else None
+    threads_cpu = 1
+    cpu_rows = int(os.environ.get("OM_BENCH_CPU_ROWS", "32"))
+    cpu_val, cpu_dt = cpu_sample(threads_cpu, cpu_rows)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded U[-1,1), splitmix64/xoshiro256**)",
+        "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "algebra": "MaxPlus<f32>",
+                   "argmax": True, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                   "l2": "flushed before each timed step (256 MiB write, untimed)"},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                "h2d_bytes_per_step": int(A.nbytes + B.nbytes),
+                "d2h_bytes_per_step": int(C.nbytes + AM.nbytes)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "fp32", "kernel": kname,
+                     "achieved": None if achieved is None else round(achieved, 2),
+                     "peak": round(FP32_PEAK_TOPS, 2), "unit": "TOP/s",
+                     "frac": None if achieved is None else round(achieved / FP32_PEAK_TOPS, 4),
+                     "peak_source": "computed: 148 SMs x 128 FP32 lanes x 2 x 1965 MHz "
+                                    "(no FP32 figure in MEASURED_PEAKS.json)",
+                     "traffic": NCU_TRAFFIC_BYTES},
+        "kernels": {k: {"ms_total": round(v[0], 4), "launches": v[1]} for k, v in prof.items()},
+        "cpu_baseline": {"value": round(cpu_val, 4), "unit": UNIT, "cores": threads_cpu,
+                         "kind": "port",
+                         "sample": f"rows 0..{cpu_rows - 1} of the workload (all columns, "
+                                   f"full k), reference loop order, {cpu_dt:.1f} s"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    be.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-check", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
+    try:
+        run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

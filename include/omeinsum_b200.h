@@ -1,0 +1,143 @@
+/*
+ * omeinsum_b200.h -- C ABI of the B200 (sm_100a) execution backend for
+ * omeinsum-rs.
+ *
+ * The entry points replace the reference's `Backend` trait for a new `B200`
+ * backend (tensor4all/omeinsum-rs, src/backend/traits.rs:42-199): a Rust
+ * `impl Backend for B200` binds them one-to-one.
+ *
+ * Conventions (same as the reference):
+ *   - tensors are column-major: axis 0 is fastest; strides count ELEMENTS;
+ *   - modes are arbitrary int32 labels, unique within one operand;
+ *   - a mode in A, B and C is a batch mode; in A and B only, contracted; in
+ *     one input and C, free; in one input only, traced (reduced first);
+ *   - outputs are written contiguous column-major in modes_c order;
+ *   - argmax (u32) is the column-major linear index over the contracted
+ *     modes, taken in modes_a order; ties go to the smallest index;
+ *   - MaxPlus zero = -FLT_MAX (f32::MIN), MinPlus zero = +FLT_MAX, MaxMul zero = 0.
+ *
+ * All device pointers are plain CUDA device addresses on the backend's device.
+ * Every call is ordered on the backend's own stream; om_b200_sync waits for it.
+ * Every function returns OM_OK (0) or an OM_ERR_* code; om_b200_last_error
+ * gives the message of the last failure on the calling thread.
+ */
+#ifndef OMEINSUM_B200_H
+#define OMEINSUM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct om_backend om_backend;
+
+/* semirings: src/algebra/standard.rs, src/algebra/tropical.rs */
+typedef enum {
+  OM_STANDARD = 0, /* (+, x)   zero 0            */
+  OM_MAXPLUS = 1,  /* (max, +) zero -FLT_MAX     */
+  OM_MINPLUS = 2,  /* (min, +) zero +FLT_MAX     */
+  OM_MAXMUL = 3    /* (max, x) zero 0            */
+} om_algebra;
+
+typedef enum { OM_F32 = 0, OM_F64 = 1, OM_U32 = 2 } om_dtype;
+
+enum {
+  OM_OK = 0,
+  OM_ERR_INVALID = 1,     /* bad argument: null pointer, bad rank, size mismatch */
+  OM_ERR_UNSUPPORTED = 2, /* dtype / algebra combination not provided            */
+  OM_ERR_CUDA = 3,        /* CUDA runtime error                                  */
+  OM_ERR_OOM = 4,         /* device allocation failed                            */
+  OM_ERR_SHAPE = 5,       /* modes / shapes inconsistent                         */
+  OM_ERR_NCCL = 6,        /* collective failed                                   */
+  OM_ERR_TIMEOUT = 7      /* a bounded wait ran out                              */
+};
+
+#define OM_MAX_DIMS 24
+
+/* Backend::name (traits.rs:50) -- returns "b200". */
+const char* om_b200_name(void);
+
+/* Copies the last error message of this thread into buf (NUL-terminated). */
+int om_b200_last_error(char* buf, size_t len);
+
+/* Creates a backend bound to CUDA device `device` with its own non-blocking
+ * stream and a stream-ordered caching allocator.  Mirrors `Cuda::on_device`
+ * (src/backend/cuda/mod.rs:258-265): a bad ordinal is an error, not a panic. */
+int om_b200_create(int device, om_backend** out);
+int om_b200_destroy(om_backend* be);
+
+/* The backend's stream (a cudaStream_t), for callers that interoperate. */
+int om_b200_stream(om_backend* be, void** stream_out);
+
+/* Backend::synchronize (traits.rs:53). */
+int om_b200_sync(om_backend* be);
+
+/* Backend::alloc (traits.rs:56): zero-filled device buffer of `bytes`. */
+int om_b200_alloc(om_backend* be, size_t bytes, void** dptr);
+int om_b200_free(om_backend* be, void* dptr);
+
+/* Backend::from_slice (traits.rs:60) is alloc + upload; Storage::to_vec
+ * (traits.rs:20) is download.  Both are stream-ordered; download waits. */
+int om_b200_upload(om_backend* be, void* dst_device, const void* src_host, size_t bytes);
+int om_b200_download(om_backend* be, void* dst_host, const void* src_device, size_t bytes);
+
+/* Backend::copy_strided (traits.rs:71-77): gathers the strided view
+ * (shape, strides, offset in elements) of src into the contiguous
+ * column-major dst.  dtype gives the element size (OM_U32 allowed). */
+int om_b200_copy_strided(om_backend* be, om_dtype dtype, const void* src, int ndim,
+                         const int64_t* shape, const int64_t* strides, int64_t offset, void* dst);
+
+/* Backend::contract (traits.rs:147-166) when argmax_out == NULL, and
+ * Backend::contract_with_argmax (traits.rs:180-199) otherwise.  The output
+ * c_out (and argmax_out) hold prod(shape_c) elements (1 when ndc == 0).
+ * Inputs are read through their strides; nothing is copied back to the host. */
+int om_b200_contract(om_backend* be, om_algebra alg, om_dtype dtype,
+                     const void* a, int nda, const int64_t* shape_a, const int64_t* strides_a,
+                     const int32_t* modes_a,
+                     const void* b, int ndb, const int64_t* shape_b, const int64_t* strides_b,
+                     const int32_t* modes_b,
+                     int ndc, const int64_t* shape_c, const int32_t* modes_c,
+                     void* c_out, uint32_t* argmax_out);
+
+/* Unary einsum ix -> iy (execute_unary_naive / execute_unary_with_argmax,
+ * src/einsum/engine.rs:752-926): trace, diagonal, reduction, permutation and
+ * diagonal embedding.  ix may repeat labels; iy may repeat labels (off-diagonal
+ * entries get the algebra's zero).  sizes_y[d] is the size of iy[d]; the input
+ * is read through shape_x/strides_x.  argmax_out (optional) receives the
+ * column-major linear input position of the winner (is_better, first wins). */
+int om_b200_unary(om_backend* be, om_algebra alg, om_dtype dtype,
+                  const void* x, int nx, const int32_t* ix, const int64_t* shape_x,
+                  const int64_t* strides_x,
+                  int ny, const int32_t* iy, const int64_t* sizes_y,
+                  void* y_out, uint32_t* argmax_out);
+
+/* Tropical backward of one binary node (src/einsum/backward.rs:90-166):
+ * scatters grad_c into grad_a / grad_b (contiguous, column-major, shapes of
+ * the normalised operands, ACCUMULATED into) through the argmax of the
+ * forward contraction.  Operands are given by shape and modes only. */
+int om_b200_tropical_backward(om_backend* be, om_dtype dtype,
+                              const void* grad_c, const uint32_t* argmax,
+                              int nda, const int64_t* shape_a, const int32_t* modes_a,
+                              int ndb, const int64_t* shape_b, const int32_t* modes_b,
+                              int ndc, const int64_t* shape_c, const int32_t* modes_c,
+                              void* grad_a, void* grad_b);
+
+/* Kernel launches issued by this thread since the last call (counter reset
+ * on read); used by benchmarks to report how many device kernels ran. */
+int64_t om_b200_launch_count(void);
+
+/* Per-kernel device timing: with profiling on, each kernel launch of this
+ * backend is bracketed by CUDA events on the backend's stream.  Turning it on
+ * clears the accumulators.  om_b200_profile_query synchronises the stream and
+ * returns, for kernel class `index` (0, 1, ...), its name, summed device time
+ * and launch count; OM_ERR_INVALID once index runs past the last class. */
+int om_b200_profile_enable(om_backend* be, int on);
+int om_b200_profile_query(om_backend* be, int index, char* name, size_t len, double* total_ms,
+                          int64_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OMEINSUM_B200_H */

@@ -1,0 +1,332 @@
+// Binary contraction planner and the om_b200_contract entry point.
+//
+// Semantics follow Backend::contract / contract_with_argmax of the reference
+// CPU backend (tensor4all/omeinsum-rs src/backend/cpu/contract.rs:467-671,
+// 752-859): modes are classified as batch / left / right / contracted
+// (classify_modes, contract.rs:11-45), labels present in one input only and
+// absent from the output are reduced first (reduce_trace_modes, :309-363),
+// and the result is contiguous column-major in modes_c order.  The argmax is
+// the column-major linear index over the contracted modes in modes_a order.
+//
+// The layout plan is B200-specific rather than the reference's
+// NoCopy/Permute/MakeContiguous choice (contract.rs:149-297): each mode group
+// (left, right, contracted, batch) is flattened to ONE affine stride per
+// operand whenever the strides allow it, in any physical order, so the GEMM
+// kernels read strided views in place; only an operand whose group cannot be
+// flattened is gathered (K1) into the GEMM's preferred layout, and only an
+// output whose groups cannot be flattened goes through a scratch buffer and a
+// permuting gather.
+#include <algorithm>
+#include <cstring>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "om_internal.h"
+
+namespace om {
+namespace {
+
+struct Operand {
+  std::vector<int32_t> modes;
+  std::vector<int64_t> shape, strides;
+  int pos(int32_t m) const {
+    for (size_t i = 0; i < modes.size(); ++i)
+      if (modes[i] == m) return (int)i;
+    return -1;
+  }
+  int64_t numel() const {
+    int64_t n = 1;
+    for (auto s : shape) n *= s;
+    return n;
+  }
+};
+
+// stride of `group` flattened in `op` in the given order, or -1
+int64_t flat_stride(const Operand& op, const std::vector<int32_t>& group) {
+  int64_t base = -1, expect = 0;
+  for (int32_t m : group) {
+    int p = op.pos(m);
+    if (op.shape[p] == 1) continue;
+    if (base < 0) {
+      base = op.strides[p];
+      expect = base * op.shape[p];
+      continue;
+    }
+    if (op.strides[p] != expect) return -1;
+    expect *= op.shape[p];
+  }
+  return base < 0 ? 0 : base;
+}
+
+std::vector<int32_t> sorted_by_stride(const Operand& op, std::vector<int32_t> g) {
+  std::stable_sort(g.begin(), g.end(), [&](int32_t x, int32_t y) {
+    return op.strides[op.pos(x)] < op.strides[op.pos(y)];
+  });
+  return g;
+}
+
+// Picks the order of a mode group that flattens in as many of `ops` as
+// possible, weighting failures by the operand's size (the cost of gathering
+// it).  With `fixed`, the given order is kept.
+std::vector<int32_t> choose_order(const std::vector<int32_t>& g,
+                                  const std::vector<const Operand*>& ops, bool fixed) {
+  if (fixed || g.size() < 2) return g;
+  std::vector<std::vector<int32_t>> cands{g};
+  for (auto* op : ops) cands.push_back(sorted_by_stride(*op, g));
+  int64_t best_cost = -1;
+  std::vector<int32_t> best = g;
+  for (auto& c : cands) {
+    int64_t cost = 0;
+    for (auto* op : ops)
+      if (flat_stride(*op, c) < 0) cost += op->numel();
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = c;
+    }
+  }
+  return best;
+}
+
+int64_t group_size(const Operand& op, const std::vector<int32_t>& g) {
+  int64_t s = 1;
+  for (int32_t m : g) s *= op.shape[op.pos(m)];
+  return s;
+}
+
+std::vector<int64_t> contiguous_strides(const std::vector<int64_t>& shape) {
+  std::vector<int64_t> st(shape.size());
+  int64_t s = 1;
+  for (size_t i = 0; i < shape.size(); ++i) {
+    st[i] = s;
+    s *= shape[i];
+  }
+  return st;
+}
+
+// Gathers `op` into a new contiguous buffer with axis order g0 ++ g1 ++ g2.
+int gather_operand(om_backend* be, size_t es, const void* src, const Operand& op,
+                   const std::vector<int32_t>& g0, const std::vector<int32_t>& g1,
+                   const std::vector<int32_t>& g2, Scratch& buf, Operand& out) {
+  std::vector<int32_t> order(g0);
+  order.insert(order.end(), g1.begin(), g1.end());
+  order.insert(order.end(), g2.begin(), g2.end());
+  std::vector<int64_t> shape, strides;
+  for (int32_t m : order) {
+    int p = op.pos(m);
+    shape.push_back(op.shape[p]);
+    strides.push_back(op.strides[p]);
+  }
+  OM_TRY(buf.alloc(be, es * (size_t)std::max<int64_t>(op.numel(), 1)));
+  OM_TRY(launch_gather(be, es, src, (int)order.size(), shape.data(), strides.data(), 0, buf.ptr));
+  out.modes = order;
+  out.shape = shape;
+  out.strides = contiguous_strides(shape);
+  return OM_OK;
+}
+
+uint64_t zero_pattern(om_algebra alg, om_dtype dt) {
+  if (dt == OM_F64) {
+    double v = alg == OM_MAXPLUS ? -1.7976931348623157e308 : (alg == OM_MINPLUS ? 1.7976931348623157e308 : 0.0);
+    uint64_t u;
+    memcpy(&u, &v, 8);
+    return u;
+  }
+  float v = alg == OM_MAXPLUS ? -3.40282347e38f : (alg == OM_MINPLUS ? 3.40282347e38f : 0.f);
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  return u;
+}
+
+}  // namespace
+
+int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Operand A,
+                  const void* b, Operand B, Operand C, void* c_out, uint32_t* argmax) {
+  const size_t es = dtype_size(dt);
+  // ---- validation ---------------------------------------------------------
+  for (const Operand* op : {&A, &B, &C}) {
+    std::set<int32_t> seen(op->modes.begin(), op->modes.end());
+    if (seen.size() != op->modes.size())
+      return set_error(OM_ERR_SHAPE,
+                       "contract: a mode repeats within one operand; take the diagonal first "
+                       "(om_b200_unary), as the einsum engine's operand normalisation does");
+    for (auto s : op->shape)
+      if (s < 0) return set_error(OM_ERR_SHAPE, "contract: negative extent");
+  }
+  auto extent_of = [&](int32_t m) -> int64_t {
+    int p = A.pos(m);
+    if (p >= 0) return A.shape[p];
+    p = B.pos(m);
+    return p >= 0 ? B.shape[p] : -1;
+  };
+  for (size_t i = 0; i < A.modes.size(); ++i) {
+    int p = B.pos(A.modes[i]);
+    if (p >= 0 && B.shape[p] != A.shape[i])
+      return set_error(OM_ERR_SHAPE, "contract: mode " + std::to_string(A.modes[i]) +
+                                         " has different extents in A and B");
+  }
+  for (size_t i = 0; i < C.modes.size(); ++i) {
+    int64_t e = extent_of(C.modes[i]);
+    if (e < 0)
+      return set_error(OM_ERR_SHAPE, "contract: output mode " + std::to_string(C.modes[i]) +
+                                         " is in neither input");
+    if (e != C.shape[i])
+      return set_error(OM_ERR_SHAPE, "contract: shape_c disagrees with the inputs for mode " +
+                                         std::to_string(C.modes[i]));
+  }
+  const int64_t nc = C.numel();
+  if (nc == 0) return OM_OK;
+  C.strides = contiguous_strides(C.shape);
+
+  // ---- classify (contract.rs:11-45) ----------------------------------------
+  std::vector<int32_t> batch, contr, lfree, rfree, ltrace, rtrace;
+  for (int32_t m : A.modes) {
+    bool inb = B.pos(m) >= 0, inc = C.pos(m) >= 0;
+    if (inb && inc) batch.push_back(m);
+    else if (inb) contr.push_back(m);
+    else if (inc) lfree.push_back(m);
+    else ltrace.push_back(m);
+  }
+  for (int32_t m : B.modes) {
+    if (A.pos(m) >= 0) continue;
+    if (C.pos(m) >= 0) rfree.push_back(m);
+    else rtrace.push_back(m);
+  }
+
+  // empty reductions: a zero extent on a traced or contracted mode
+  if (A.numel() == 0 || B.numel() == 0) {
+    OM_TRY(launch_fill(be, c_out, es, nc, zero_pattern(alg, dt)));
+    if (argmax) OM_TRY(launch_fill(be, argmax, 4, nc, 0));
+    return OM_OK;
+  }
+
+  // ---- trace reduction (reduce_trace_modes, contract.rs:309-363) ----------
+  Scratch ta, tb;
+  auto reduce = [&](const void*& ptr, Operand& op, const std::vector<int32_t>& tr,
+                    Scratch& buf) -> int {
+    if (tr.empty()) return OM_OK;
+    Operand r;
+    for (size_t i = 0; i < op.modes.size(); ++i) {
+      if (std::find(tr.begin(), tr.end(), op.modes[i]) != tr.end()) continue;
+      r.modes.push_back(op.modes[i]);
+      r.shape.push_back(op.shape[i]);
+    }
+    r.strides = contiguous_strides(r.shape);
+    OM_TRY(buf.alloc(be, es * (size_t)std::max<int64_t>(r.numel(), 1)));
+    OM_TRY(launch_unary(be, alg, dt, ptr, (int)op.modes.size(), op.modes.data(), op.shape.data(),
+                        op.strides.data(), (int)r.modes.size(), r.modes.data(), r.shape.data(),
+                        buf.ptr, nullptr));
+    ptr = buf.ptr;
+    op = r;
+    return OM_OK;
+  };
+  OM_TRY(reduce(a, A, ltrace, ta));
+  OM_TRY(reduce(b, B, rtrace, tb));
+
+  // ---- group orders ---------------------------------------------------------
+  const bool track = argmax != nullptr;
+  contr = choose_order(contr, {&A, &B}, track);  // argmax index is in modes_a order
+  lfree = choose_order(lfree, {&A, &C}, false);
+  rfree = choose_order(rfree, {&B, &C}, false);
+  batch = choose_order(batch, {&A, &B, &C}, false);
+
+  Scratch ga, gb;
+  if (flat_stride(A, lfree) < 0 || flat_stride(A, contr) < 0 || flat_stride(A, batch) < 0) {
+    Operand g;
+    OM_TRY(gather_operand(be, es, a, A, lfree, contr, batch, ga, g));
+    a = ga.ptr;
+    A = g;
+  }
+  if (flat_stride(B, contr) < 0 || flat_stride(B, rfree) < 0 || flat_stride(B, batch) < 0) {
+    Operand g;
+    OM_TRY(gather_operand(be, es, b, B, contr, rfree, batch, gb, g));
+    b = gb.ptr;
+    B = g;
+  }
+
+  GemmArgs g{};
+  g.alg = alg;
+  g.dtype = dt;
+  g.M = group_size(A, lfree);
+  g.K = group_size(A, contr);
+  g.N = group_size(B, rfree);
+  g.batch = group_size(A, batch);
+  g.A = a;
+  g.sam = flat_stride(A, lfree);
+  g.sak = flat_stride(A, contr);
+  g.sab = flat_stride(A, batch);
+  g.B = b;
+  g.sbk = flat_stride(B, contr);
+  g.sbn = flat_stride(B, rfree);
+  g.sbb = flat_stride(B, batch);
+
+  const bool c_direct =
+      flat_stride(C, lfree) >= 0 && flat_stride(C, rfree) >= 0 && flat_stride(C, batch) >= 0;
+  Scratch cs, as;
+  if (c_direct) {
+    g.C = c_out;
+    g.argmax = argmax;
+    g.scm = flat_stride(C, lfree);
+    g.scn = flat_stride(C, rfree);
+    g.scb = flat_stride(C, batch);
+  } else {
+    OM_TRY(cs.alloc(be, es * (size_t)nc));
+    if (argmax) OM_TRY(as.alloc(be, 4 * (size_t)nc));
+    g.C = cs.ptr;
+    g.argmax = argmax ? (uint32_t*)as.ptr : nullptr;
+    g.scm = 1;
+    g.scn = g.M;
+    g.scb = g.M * g.N;
+  }
+  OM_TRY(launch_gemm(be, g));
+
+  if (!c_direct) {
+    // scratch holds [lfree, rfree, batch]; permute into modes_c order
+    std::vector<int32_t> cur(lfree);
+    cur.insert(cur.end(), rfree.begin(), rfree.end());
+    cur.insert(cur.end(), batch.begin(), batch.end());
+    std::vector<int64_t> cur_shape;
+    for (int32_t m : cur) cur_shape.push_back(C.shape[C.pos(m)]);
+    std::vector<int64_t> cur_st = contiguous_strides(cur_shape);
+    std::vector<int64_t> shp, st;
+    for (int32_t m : C.modes) {
+      int q = (int)(std::find(cur.begin(), cur.end(), m) - cur.begin());
+      shp.push_back(cur_shape[q]);
+      st.push_back(cur_st[q]);
+    }
+    OM_TRY(launch_gather(be, es, cs.ptr, (int)shp.size(), shp.data(), st.data(), 0, c_out));
+    if (argmax)
+      OM_TRY(launch_gather(be, 4, as.ptr, (int)shp.size(), shp.data(), st.data(), 0, argmax));
+  }
+  return OM_OK;
+}
+
+}  // namespace om
+
+extern "C" int om_b200_contract(om_backend* be, om_algebra alg, om_dtype dtype, const void* a,
+                                int nda, const int64_t* shape_a, const int64_t* strides_a,
+                                const int32_t* modes_a, const void* b, int ndb,
+                                const int64_t* shape_b, const int64_t* strides_b,
+                                const int32_t* modes_b, int ndc, const int64_t* shape_c,
+                                const int32_t* modes_c, void* c_out, uint32_t* argmax_out) {
+  using namespace om;
+  if (!be || !a || !b || !c_out) return set_error(OM_ERR_INVALID, "om_b200_contract: null pointer");
+  if (nda < 0 || ndb < 0 || ndc < 0 || nda > OM_MAX_DIMS || ndb > OM_MAX_DIMS || ndc > OM_MAX_DIMS)
+    return set_error(OM_ERR_INVALID, "om_b200_contract: rank out of range");
+  if ((nda && (!shape_a || !strides_a || !modes_a)) || (ndb && (!shape_b || !strides_b || !modes_b)) ||
+      (ndc && (!shape_c || !modes_c)))
+    return set_error(OM_ERR_INVALID, "om_b200_contract: null shape/stride/mode array");
+  if (dtype != OM_F32 && dtype != OM_F64)
+    return set_error(OM_ERR_UNSUPPORTED, "om_b200_contract: dtype must be OM_F32 or OM_F64");
+  OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  Operand A, B, C;
+  A.modes.assign(modes_a, modes_a + nda);
+  A.shape.assign(shape_a, shape_a + nda);
+  A.strides.assign(strides_a, strides_a + nda);
+  B.modes.assign(modes_b, modes_b + ndb);
+  B.shape.assign(shape_b, shape_b + ndb);
+  B.strides.assign(strides_b, strides_b + ndb);
+  C.modes.assign(modes_c, modes_c + ndc);
+  C.shape.assign(shape_c, shape_c + ndc);
+  return contract_impl(be, alg, dtype, a, A, b, B, C, c_out, argmax_out);
+}

@@ -1,0 +1,271 @@
+"""Parity of the B200 contraction (through the C ABI) with the CPU restatement
+of the reference (oracle/) and with the reference's own known answers.
+
+Tropical algebras: values and argmax bit-exact.  Standard algebra: the
+reference uses faer (summation order unknown), so Standard is checked
+against the oracle's extended-precision sum with the GEMM error bound
+    |x - r| <= tol * sum_k |a_ik| |b_kj|,   tol = 1e-5 (f32), 1e-12 (f64).
+"""
+import numpy as np
+import pytest
+
+import oracle as orc
+from conftest import load_pkg
+from test_oracle_kats import KATS, arr, check_kat
+
+pytestmark = pytest.mark.gpu
+
+TOL = {np.float32: 1e-5, np.float64: 1e-12}
+
+
+@pytest.fixture(scope="module")
+def be():
+    om = load_pkg()
+    b = om.B200(0)
+    yield b
+    b.close()
+
+
+def dev_contract(be, alg, a, sa, ta, ma, b, sb, tb, mb, sc, mc, argmax):
+    A, B = be.from_slice(a), be.from_slice(b)
+    if argmax:
+        c, am = be.contract_with_argmax(alg, A, sa, ta, ma, B, sb, tb, mb, sc, mc)
+        return c.to_vec(), am.to_vec()
+    return be.contract(alg, A, sa, ta, ma, B, sb, tb, mb, sc, mc).to_vec(), None
+
+
+def bits_equal(x, y):
+    """Bitwise equality, except that any NaN matches any NaN: the payload and
+    sign of a NaN made by inf - inf or 0 * inf are set by the FPU (x86 gives
+    0xffc00000, the GPU 0x7fffffff), not by the algorithm."""
+    x, y = np.asarray(x), np.asarray(y)
+    if x.dtype in (np.float32, np.float64):
+        u = np.uint32 if x.dtype == np.float32 else np.uint64
+        nx, ny = np.isnan(x), np.isnan(y)
+        return np.array_equal(nx, ny) and np.array_equal(x[~nx].view(u), y[~ny].view(u))
+    return np.array_equal(x, y)
+
+
+def check_case(be, alg, a, sa, ta, ma, b, sb, tb, mb, sc, mc, argmax=True):
+    c, am = dev_contract(be, alg, a, sa, ta, ma, b, sb, tb, mb, sc, mc, argmax)
+    r = orc.contract(alg, a, sa, ta, ma, b, sb, tb, mb, sc, mc, argmax=argmax)
+    rc, ram = (r if argmax else (r, None))
+    if alg == "standard":
+        bound = orc.contract("standard", np.abs(a), sa, ta, ma, np.abs(b), sb, tb, mb, sc, mc)
+        tol = TOL[a.dtype.type]
+        err = np.abs(c.astype(np.float64) - rc.astype(np.float64))
+        assert np.all(err <= tol * bound + 1e-300), float(np.max(err / (bound + 1e-300)))
+        if argmax:
+            assert np.all(am == 0)
+    else:
+        if not bits_equal(c, rc):
+            u = np.uint32 if c.dtype == np.float32 else np.uint64
+            bad = np.nonzero((c.view(u) != rc.view(u)) & ~(np.isnan(c) & np.isnan(rc)))[0]
+            raise AssertionError(f"{len(bad)} value mismatches, first at {bad[:5]}: "
+                                 f"dev {c[bad[:5]]} ref {rc[bad[:5]]}")
+        if argmax:
+            bad = np.nonzero(am != ram)[0]
+            assert len(bad) == 0, f"{len(bad)} argmax mismatches at {bad[:5]}: " \
+                                  f"dev {am[bad[:5]]} ref {ram[bad[:5]]}"
+
+
+def col(shape):
+    return orc.col_strides(shape)
+
+
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("k", KATS, ids=[k["name"] for k in KATS])
+def test_reference_kat_on_device(be, k):
+    dt = np.float32 if k["dtype"] == "f32" else np.float64
+    if k["kind"] == "copy_strided":
+        s = be.from_slice(arr(k["src"], dt))
+        out = be.copy_strided(s, k["shape"], k["strides"], k["offset"]).to_vec()
+        check_kat(k, out, None)
+        return
+    a, b = arr(k["a"], dt), arr(k["b"], dt)
+    c, am = dev_contract(be, k["alg"], a, k["shape_a"], k["strides_a"], k["modes_a"], b,
+                         k["shape_b"], k["strides_b"], k["modes_b"], k["shape_c"], k["modes_c"],
+                         k.get("with_argmax", False))
+    check_kat(k, c, am)
+    # and the device agrees with the oracle on every KAT, asserted or not
+    check_case(be, k["alg"], a, k["shape_a"], k["strides_a"], k["modes_a"], b, k["shape_b"],
+               k["strides_b"], k["modes_b"], k["shape_c"], k["modes_c"],
+               argmax=k.get("with_argmax", False) and k["alg"] != "standard")
+
+
+MATMUL_SIZES = [(1, 1, 1), (3, 5, 7), (64, 32, 64), (130, 97, 129), (256, 512, 192),
+                (128, 1000, 256)]
+
+
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul", "standard"])
+@pytest.mark.parametrize("mkn", MATMUL_SIZES, ids=[f"{m}x{k}x{n}" for m, k, n in MATMUL_SIZES])
+@pytest.mark.parametrize("argmax", [True, False])
+def test_matmul_uniform_f32(be, alg, mkn, argmax):
+    m, k, n = mkn
+    a = orc.uniform(11 + m, m * k)
+    b = orc.uniform(977 + n, k * n)
+    if alg == "maxmul":
+        a, b = np.abs(a), np.abs(b)
+    check_case(be, alg, a, [m, k], [1, m], [0, 1], b, [k, n], [1, k], [1, 2], [m, n], [0, 2],
+               argmax=argmax and alg != "standard")
+
+
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul"])
+@pytest.mark.parametrize("mkn", [(64, 64, 64), (192, 256, 320), (257, 130, 131)])
+def test_matmul_ties_first_k_wins(be, alg, mkn):
+    m, k, n = mkn
+    a = orc.ties(5, m * k, -2, 2)
+    b = orc.ties(6, k * n, -2, 2)
+    if alg == "maxmul":
+        a, b = np.abs(a) + 1, np.abs(b)
+    check_case(be, alg, a, [m, k], [1, m], [0, 1], b, [k, n], [1, k], [1, 2], [m, n], [0, 2])
+
+
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul"])
+@pytest.mark.parametrize("special", ["neg_inf_cols", "pos_inf", "nan", "neg_zero", "both_inf",
+                                     "all_neg_inf"])
+def test_special_values(be, alg, special):
+    m, k, n = 128, 96, 136
+    a = orc.uniform(1, m * k).reshape(k, m).T.copy()  # (m,k) then flatten col-major below
+    b = orc.uniform(2, k * n).reshape(n, k).T.copy()
+    if special == "neg_inf_cols":
+        a[:, 3] = -np.inf
+        a[:, 50:52] = -np.inf
+        b[7, :] = -np.inf
+    elif special == "pos_inf":
+        a[5, :] = np.inf
+        b[:, 9] = np.inf
+    elif special == "nan":
+        a[3, 4] = np.nan
+        b[10, 17] = np.nan
+    elif special == "neg_zero":
+        a[:, :] = 0.0
+        a[1::2, :] = -0.0
+        b[:, :] = -0.0
+    elif special == "both_inf":
+        a[0, :] = np.inf
+        b[:, 0] = -np.inf
+    elif special == "all_neg_inf":
+        a[:, :] = -np.inf
+    af = np.asfortranarray(a).reshape(-1, order="F").astype(np.float32)
+    bf = np.asfortranarray(b).reshape(-1, order="F").astype(np.float32)
+    check_case(be, alg, af, [m, k], [1, m], [0, 1], bf, [k, n], [1, k], [1, 2], [m, n], [0, 2])
+
+
+LAYOUTS = {
+    # name: (modes_a, modes_b, modes_c) over labels i=0, j=1, k=2 with extents
+    "ij,jk->ik": ([0, 1], [1, 2], [0, 2]),
+    "ji,jk->ik": ([1, 0], [1, 2], [0, 2]),
+    "ij,kj->ik": ([0, 1], [2, 1], [0, 2]),
+    "ji,kj->ki": ([1, 0], [2, 1], [2, 0]),
+    "ij,jk->ki": ([0, 1], [1, 2], [2, 0]),
+}
+
+
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "standard"])
+@pytest.mark.parametrize("name", list(LAYOUTS))
+def test_operand_orientations(be, alg, name):
+    ext = {0: 96, 1: 160, 2: 128}
+    ma, mb, mc = LAYOUTS[name]
+    sa, sb, sc = [ext[x] for x in ma], [ext[x] for x in mb], [ext[x] for x in mc]
+    a = orc.uniform(21, int(np.prod(sa)))
+    b = orc.uniform(22, int(np.prod(sb)))
+    check_case(be, alg, a, sa, col(sa), ma, b, sb, col(sb), mb, sc, mc,
+               argmax=alg != "standard")
+
+
+@pytest.mark.parametrize("alg", ["standard", "minplus", "maxplus"])
+def test_permuted_config2_small(be, alg):
+    # 'abcd,dcef->abfe' (the BASELINE Standard / MinPlus config) at a=b=e=f=8, c=d=4
+    a_, c_ = 8, 4
+    A = orc.normal(31, a_ * a_ * c_ * c_)
+    B = orc.normal(32, c_ * c_ * a_ * a_)
+    sa, sb = [a_, a_, c_, c_], [c_, c_, a_, a_]
+    check_case(be, alg, A, sa, col(sa), [0, 1, 2, 3], B, sb, col(sb), [3, 2, 4, 5],
+               [a_, a_, a_, a_], [0, 1, 5, 4], argmax=alg != "standard")
+
+
+@pytest.mark.parametrize("alg", ["standard", "maxplus"])
+def test_strided_views(be, alg):
+    # sub-matrix views with padding between columns and a transposed B view
+    m, k, n, lda, ldb = 70, 90, 80, 75, 100
+    a = orc.uniform(41, lda * k)
+    b = orc.uniform(42, ldb * k)
+    check_case(be, alg, a, [m, k], [1, lda], [0, 1], b, [k, n], [ldb, 1], [1, 2], [m, n], [0, 2],
+               argmax=alg != "standard")
+
+
+@pytest.mark.parametrize("alg", ["standard", "maxplus", "minplus", "maxmul"])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_batched_and_trace(be, alg, dtype):
+    # 'bijx,bjky->kib' : batch b, contracted j, traced x (A) and y (B)
+    e = {0: 3, 1: 5, 2: 6, 3: 4, 4: 2, 5: 3}
+    ma, mb, mc = [0, 1, 2, 4], [0, 2, 3, 5], [3, 1, 0]
+    sa, sb, sc = [e[x] for x in ma], [e[x] for x in mb], [e[x] for x in mc]
+    a = orc.uniform(51, int(np.prod(sa)), dtype)
+    b = orc.uniform(52, int(np.prod(sb)), dtype)
+    if alg == "maxmul":
+        a, b = np.abs(a), np.abs(b)
+    check_case(be, alg, a, sa, col(sa), ma, b, sb, col(sb), mb, sc, mc, argmax=alg != "standard")
+
+
+@pytest.mark.parametrize("alg", ["standard", "maxplus", "minplus", "maxmul"])
+def test_f64_matmul(be, alg):
+    m, k, n = 100, 120, 90
+    a = orc.uniform(61, m * k, np.float64)
+    b = orc.uniform(62, k * n, np.float64)
+    if alg == "maxmul":
+        a, b = np.abs(a), np.abs(b)
+    check_case(be, alg, a, [m, k], [1, m], [0, 1], b, [k, n], [1, k], [1, 2], [m, n], [0, 2],
+               argmax=alg != "standard")
+
+
+def test_network_like_hyperedges(be):
+    # bond-dimension-2 node with many batch modes: 'abcdef,cdefgh->abgh' style
+    ma, mb, mc = [0, 1, 2, 3, 4, 5, 6, 7], [2, 3, 4, 5, 6, 7, 8, 9], [0, 1, 4, 5, 8, 9]
+    sa, sb = [2] * 8, [2] * 8
+    a = orc.ties(71, 256, -3, 3)
+    b = orc.ties(72, 256, -3, 3)
+    a[::7] = -np.inf
+    check_case(be, "maxplus", a, sa, col(sa), ma, b, sb, col(sb), mb, [2] * 6, mc)
+
+
+def test_scalar_output_and_outer(be):
+    a = orc.uniform(81, 300)
+    b = orc.uniform(82, 300)
+    check_case(be, "maxplus", a, [300], [1], [0], b, [300], [1], [0], [], [])
+    check_case(be, "minplus", a[:40], [40], [1], [0], b[:30], [30], [1], [1], [40, 30], [0, 1])
+
+
+def test_errors_are_status_codes(be):
+    om = load_pkg()
+    a = be.from_slice(np.ones(4, np.float32))
+    with pytest.raises(om.OmError, match="extent"):
+        be.contract("maxplus", a, [2, 2], [1, 2], [0, 1], a, [4], [1], [1], [2], [0])
+    with pytest.raises(om.OmError, match="repeats"):
+        be.contract("maxplus", a, [2, 2], [1, 2], [0, 0], a, [2, 2], [1, 2], [0, 1], [2], [1])
+
+
+def test_headline_2048_maxplus_argmax(be):
+    """BASELINE config 1 at full size: MaxPlus 'ij,jk->ik', 2048^3, argmax.
+    Checked against the oracle on 48 sampled rows (all 2048 columns), plus
+    size-independent properties over the whole output."""
+    m = k = n = 2048
+    a = orc.uniform(0x5EED, m * k)
+    b = orc.uniform(0x5EED + 1, k * n)
+    c, am = dev_contract(be, "maxplus", a, [m, k], [1, m], [0, 1], b, [k, n], [1, k], [1, 2],
+                         [m, n], [0, 2], True)
+    C = c.reshape(n, m).T
+    AM = am.reshape(n, m).T
+    Am = a.reshape(k, m).T
+    Bm = b.reshape(n, k).T
+    rows = np.linspace(0, m - 1, 48).astype(int)
+    sub = np.asfortranarray(Am[rows, :]).reshape(-1, order="F")
+    rc, ram = orc.gemm("maxplus", sub, b, len(rows), k, n, argmax=True, threads=orc.max_threads())
+    assert bits_equal(C[rows, :].reshape(-1, order="F"), rc)
+    np.testing.assert_array_equal(AM[rows, :].reshape(-1, order="F"), ram)
+    # properties everywhere: the value is attained at the argmax, and argmax < k
+    assert AM.max() < k
+    jj = np.arange(n)[None, :]
+    attained = (Am[np.arange(m)[:, None], AM] + Bm[AM, jj]).astype(np.float32)
+    assert bits_equal(attained, C)
