@@ -38,9 +38,14 @@ OPS = 2.0 * M * N * K  # one (x) and one (+) per (i, j, k)
 METRIC = "tropical semiring GOP/s (binary contract)"
 UNIT = "GOP/s"
 WORKLOAD = "maxplus_f32_ij_jk_ik_2048x2048x2048_argmax"
-# FP32 CUDA-core peak (no measured figure exists for it in MEASURED_PEAKS.json):
-# 148 SMs x 128 lanes x 2 ops x 1965 MHz (max SM clock).
+# FP32 CUDA-core peak (MEASURED_PEAKS.json has no FP32 figure): 148 SMs x 128
+# FP32 lanes x 2 (an FFMA counts as two operations) x 1965 MHz max SM clock.
 FP32_PEAK_TOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+# Measured ceiling of the instruction pair the kernel is built on (one packed
+# add.f32x2 + one 3-input max.f32 = 2 (+, max) steps = 4 operations) in a
+# register-only loop: 39 pairs/clk/SM at 1965 MHz
+# (profiles/tropical_instruction_mix.md).
+PAIR_CEILING_TOPS = 148 * 39 * 4 * 1.965e9 / 1e12
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
 # kernel, from the ncu capture summarised in profiles/ (None until captured).
 NCU_TRAFFIC_BYTES = None
@@ -132,7 +137,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     threads = orc.max_threads()
-    rows = max(8, min(M, int(os.environ.get("OM_BENCH_REF_ROWS", "64"))))
+    rows = max(8, min(M, int(os.environ.get("OM_BENCH_REF_ROWS", str(min(M, 32 * threads))))))
     for _ in range(args.warmup):
         cpu_sample(threads, max(8, rows // 8))
     vals, total = [], 0.0
@@ -256,7 +261,7 @@ def run_b200(args, rank, world, local_rank):
     kname, (kms, kn) = top
     achieved = OPS / (kms / kn / 1e3) / 1e12 if kn and kms else None
     threads_cpu = 1
-    cpu_rows = int(os.environ.get("OM_BENCH_CPU_ROWS", "32"))
+    cpu_rows = int(os.environ.get("OM_BENCH_CPU_ROWS", str(M)))
     cpu_val, cpu_dt = cpu_sample(threads_cpu, cpu_rows)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
@@ -276,6 +281,9 @@ def run_b200(args, rank, world, local_rank):
                      "frac": None if achieved is None else round(achieved / FP32_PEAK_TOPS, 4),
                      "peak_source": "computed: 148 SMs x 128 FP32 lanes x 2 x 1965 MHz "
                                     "(no FP32 figure in MEASURED_PEAKS.json)",
+                     "instruction_ceiling": round(PAIR_CEILING_TOPS, 2),
+                     "frac_of_instruction_ceiling": None if achieved is None
+                     else round(achieved / PAIR_CEILING_TOPS, 4),
                      "traffic": NCU_TRAFFIC_BYTES},
         "kernels": {k: {"ms_total": round(v[0], 4), "launches": v[1]} for k, v in prof.items()},
         "cpu_baseline": {"value": round(cpu_val, 4), "unit": UNIT, "cores": threads_cpu,

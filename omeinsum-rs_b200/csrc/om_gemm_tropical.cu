@@ -6,22 +6,29 @@
 // or -0 (checked on the device by a special-value scan; otherwise the exact
 // compare-select kernel runs, gated on the same flag word, with no host sync).
 //
-// Design (CUDA cores; tensor cores have no max/min).  A semiring step is one
-// FADD (or FMUL) and one FMNMX; on B200 both issue at one warp-instruction per
-// scheduler per clock, and the packed add.f32x2 / 3-input max.f32 forms run at
-// half rate, so they save nothing.  The kernel therefore aims at the issue
-// ceiling of 2 instructions per (i, j, k):
-//   * CTA tile 128 x 64, 256 threads, 8 x 4 outputs per thread (2 CTAs/SM),
-//     k slabs of 32 double-buffered in shared memory through registers, so any
-//     of the four unit-stride orientations of A and B is read with 16-byte
-//     loads; per k a thread issues 3 LDS.128 and 32 (FADD, FMNMX) pairs;
-//   * argmax without a per-k compare-select: after each slab one compare per
-//     output marks (in shared memory) the slab in which the running max
-//     strictly improved.  The last such slab holds the first k reaching the
-//     final max, because every earlier slab's max is strictly smaller.  A
-//     resolve pass re-stages each slab and scans only the outputs it decides
-//     for the first k with a (x) b == max, so ties go to the smallest k, and
-//     outputs that never beat zero() keep argmax 0, as in the reference.
+// Design (CUDA cores; tensor cores have no max/min).  One semiring step is an
+// add (or multiply) and a max (or min).  Shared memory holds k-PAIRS (element
+// (m, k..k+1) is one float2), so one packed `add.rn.f32x2` forms two products
+// and one 3-input `max.f32` folds both into the accumulator: 2 instructions
+// per 2 (i, j, k).  On B200 both forms occupy their pipe for two passes, but
+// they need half the issue slots of scalar FADD + FMNMX, which leaves room
+// for the fragment loads; measured, this form is about 25% faster.
+//   * CTA tile 128 x 64, 256 threads, 8 x 4 outputs per thread (two CTAs per
+//     SM), k slabs of 32 double-buffered in shared memory through registers,
+//     so any of the four unit-stride orientations of A and B is read with
+//     16-byte loads;
+//   * lane layouts for which every fragment LDS.128 of a warp touches one
+//     128-byte shared-memory line.
+//
+// Argmax without a per-k compare-select: after each slab one compare per
+// output sets a bit when the running max strictly improved inside the slab;
+// the 32-bit mask of a thread is written to a global workspace.  The last
+// slab with the bit set holds the first k reaching the final max, because
+// every earlier slab's max is strictly smaller.  A resolve pass walks the
+// slabs backwards, re-stages each one with cp.async (two stages), and scans
+// only the outputs it decides (compacted across the warp) for the first k
+// with a (x) b == max; ties go to the smallest k and outputs that never beat
+// zero() keep argmax 0, as in the reference.
 #include <algorithm>
 
 #include "om_internal.h"
@@ -32,13 +39,41 @@ namespace {
 
 constexpr int TB_M = 128, TB_N = 64, TB_K = 32, NT = 256, NE = 32;
 
+__device__ __forceinline__ unsigned long long pk_add(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long pk_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ void unpack(unsigned long long s, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(s));
+}
+
 template <int ALG>
 __device__ __forceinline__ float tmul(float a, float b) {
   return ALG == OM_MAXMUL ? a * b : a + b;
 }
 template <int ALG>
-__device__ __forceinline__ float tfold(float acc, float p) {
-  return ALG == OM_MINPLUS ? fminf(acc, p) : fmaxf(acc, p);
+__device__ __forceinline__ unsigned long long tmul2(unsigned long long a, unsigned long long b) {
+  return ALG == OM_MAXMUL ? pk_mul(a, b) : pk_add(a, b);
+}
+template <int ALG>
+__device__ __forceinline__ float tfold3(float acc, float x, float y) {
+  return ALG == OM_MINPLUS ? min3f(acc, x, y) : max3f(acc, x, y);
 }
 template <int ALG>
 __device__ __forceinline__ bool improved(float now, float before) {
@@ -65,8 +100,14 @@ struct FastArgs {
   uint32_t* ws;  // argmax: per-CTA, per-slab, per-thread improvement bitmasks
 };
 
-// Stages one 128 x 32 slab of A into As[k][m] and one 32 x 64 slab of B into
-// Bs[k][n] through registers.
+// float index of element (row, k) in a k-pair slab of width W
+template <int W>
+__device__ __forceinline__ int at(int row, int k) {
+  return ((k >> 1) * W + row) * 2 + (k & 1);
+}
+
+// Stages one 128 x 32 slab of A and one 32 x 64 slab of B through registers
+// (16 floats of A and 8 of B per thread) into the k-pair layout.
 template <int ALG, bool A_MC, bool B_KC>
 struct Stager {
   float4 ra[4], rb[2];
@@ -77,12 +118,13 @@ struct Stager {
     const float4 padv = make_float4(pad, pad, pad, pad);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const int u = tid + r * NT;
-      if (A_MC) {  // A[m + k*lda]: unit (k, 4 m)
-        const int mq = u % 32, kk = u / 32;
-        const int m = m0 + mq * 4, k = k0 + kk;
+      if (A_MC) {  // A[m + k*lda]: 512 (k-pair, m-quad) units, rows 2p and 2p+1
+        const int q = (r >> 1) * NT + tid;
+        const int mq = q % 32, kp = q / 32;
+        const int m = m0 + mq * 4, k = k0 + 2 * kp + (r & 1);
         ra[r] = (m < g.M && k < g.K) ? *(const float4*)(Ab + m + (int64_t)k * g.lda) : padv;
-      } else {  // A[m*lda + k]: unit (m, 4 k)
+      } else {  // A[m*lda + k]: unit = 4 k at one m
+        const int u = tid + r * NT;
         const int mm = u % TB_M, kq = u / TB_M;
         const int m = m0 + mm, k = k0 + kq * 4;
         ra[r] = (m < g.M && k < g.K) ? *(const float4*)(Ab + (int64_t)m * g.lda + k) : padv;
@@ -90,14 +132,14 @@ struct Stager {
     }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      const int u = tid + r * NT;
-      if (B_KC) {  // B[k + n*ldb]: unit (n, 4 k)
+      if (B_KC) {  // B[k + n*ldb]: unit = 4 k at one n
+        const int u = tid + r * NT;
         const int nn = u % TB_N, kq = u / TB_N;
         const int n = n0 + nn, k = k0 + kq * 4;
         rb[r] = (n < g.N && k < g.K) ? *(const float4*)(Bb + (int64_t)n * g.ldb + k) : padv;
-      } else {  // B[k*ldb + n]: unit (k, 4 n)
-        const int nq = u % 16, kk = u / 16;
-        const int n = n0 + nq * 4, k = k0 + kk;
+      } else {  // B[k*ldb + n]: 256 (k-pair, n-quad) units, rows 2p and 2p+1
+        const int nq = tid % 16, kp = tid / 16;
+        const int n = n0 + nq * 4, k = k0 + 2 * kp + r;
         rb[r] = (n < g.N && k < g.K) ? *(const float4*)(Bb + n + (int64_t)k * g.ldb) : padv;
       }
     }
@@ -106,59 +148,130 @@ struct Stager {
   __device__ __forceinline__ void store(float* As, float* Bs, int tid) {
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const int u = tid + r * NT;
       if (A_MC) {
-        const int mq = u % 32, kk = u / 32;
-        *(float4*)(As + kk * TB_M + mq * 4) = ra[r];
+        if (r & 1) {
+          const int q = (r >> 1) * NT + tid;
+          const int mq = q % 32, kp = q / 32;
+          const float4 x0 = ra[r - 1], x1 = ra[r];
+          float4* d = (float4*)(As + at<TB_M>(mq * 4, 2 * kp));
+          d[0] = make_float4(x0.x, x1.x, x0.y, x1.y);
+          d[1] = make_float4(x0.z, x1.z, x0.w, x1.w);
+        }
       } else {
+        const int u = tid + r * NT;
         const int mm = u % TB_M, kq = u / TB_M;
-        As[(4 * kq + 0) * TB_M + mm] = ra[r].x;
-        As[(4 * kq + 1) * TB_M + mm] = ra[r].y;
-        As[(4 * kq + 2) * TB_M + mm] = ra[r].z;
-        As[(4 * kq + 3) * TB_M + mm] = ra[r].w;
+        *(float2*)(As + at<TB_M>(mm, 4 * kq)) = make_float2(ra[r].x, ra[r].y);
+        *(float2*)(As + at<TB_M>(mm, 4 * kq + 2)) = make_float2(ra[r].z, ra[r].w);
       }
     }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      const int u = tid + r * NT;
       if (B_KC) {
+        const int u = tid + r * NT;
         const int nn = u % TB_N, kq = u / TB_N;
-        Bs[(4 * kq + 0) * TB_N + nn] = rb[r].x;
-        Bs[(4 * kq + 1) * TB_N + nn] = rb[r].y;
-        Bs[(4 * kq + 2) * TB_N + nn] = rb[r].z;
-        Bs[(4 * kq + 3) * TB_N + nn] = rb[r].w;
-      } else {
-        const int nq = u % 16, kk = u / 16;
-        *(float4*)(Bs + kk * TB_N + nq * 4) = rb[r];
+        *(float2*)(Bs + at<TB_N>(nn, 4 * kq)) = make_float2(rb[r].x, rb[r].y);
+        *(float2*)(Bs + at<TB_N>(nn, 4 * kq + 2)) = make_float2(rb[r].z, rb[r].w);
+      } else if (r == 1) {
+        const int nq = tid % 16, kp = tid / 16;
+        const float4 x0 = rb[0], x1 = rb[1];
+        float4* d = (float4*)(Bs + at<TB_N>(nq * 4, 2 * kp));
+        d[0] = make_float4(x0.x, x1.x, x0.y, x1.y);
+        d[1] = make_float4(x0.z, x1.z, x0.w, x1.w);
       }
     }
   }
 };
 
-// Thread (tx, ty) owns rows m = 4*tx + (i & 3) + 64*(i >> 2) (i < 8) and
-// columns n = 4*ty + j (j < 4).  A warp spans 8 consecutive tx and 4
-// consecutive ty, so each of its LDS.128 fragment loads touches one 128-byte
-// line of shared memory (one wavefront).
-__device__ __forceinline__ int row_of(int tx, int i) { return 4 * tx + (i & 3) + 64 * (i >> 2); }
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(gmem),
+               "r"(valid ? 16 : 0));
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N));
+}
+
+// Re-stages a slab for the argmax resolve pass in the operands' natural
+// layout: A as [k][m] (m-contiguous A) or [m][k]; B as [n][k] (k-contiguous
+// B) or [k][n].  k-contiguous rows are padded to 36 floats so that lanes
+// scanning different rows at the same k hit different banks.  Out-of-range
+// chunks are zero-filled; the scan never reads them because it stops at K and
+// only visits in-range outputs.
+template <bool A_MC, bool B_KC>
+struct ResolveStager {
+  static constexpr int LD = TB_K + 4;
+  static constexpr int A_FLOATS = A_MC ? TB_K * TB_M : TB_M * LD;
+  static constexpr int B_FLOATS = B_KC ? TB_N * LD : TB_K * TB_N;
+  static constexpr int STAGE = A_FLOATS + B_FLOATS;
+  __device__ static __forceinline__ int a_at(int m, int k) { return A_MC ? k * TB_M + m : m * LD + k; }
+  __device__ static __forceinline__ int b_at(int n, int k) { return B_KC ? n * LD + k : k * TB_N + n; }
+
+  __device__ __forceinline__ void issue(const FastArgs& g, const float* Ab, const float* Bb, int m0,
+                                        int n0, int t, float* RA, float* RB, int tid) {
+    const int k0 = t * TB_K;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int c = tid + r * NT;
+      const int m = A_MC ? 4 * (c % 32) : c / 8;
+      const int k = A_MC ? c / 32 : 4 * (c % 8);
+      const bool ok = (m0 + m < g.M) && (k0 + k < g.K);
+      const float* src = ok ? (A_MC ? Ab + (m0 + m) + (int64_t)(k0 + k) * g.lda
+                                    : Ab + (int64_t)(m0 + m) * g.lda + (k0 + k))
+                            : Ab;
+      cp_async16(RA + a_at(m, k), src, ok);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int c = tid + r * NT;
+      const int n = B_KC ? c / 8 : 4 * (c % 16);
+      const int k = B_KC ? 4 * (c % 8) : c / 16;
+      const bool ok = (n0 + n < g.N) && (k0 + k < g.K);
+      const float* src = ok ? (B_KC ? Bb + (int64_t)(n0 + n) * g.ldb + (k0 + k)
+                                    : Bb + (n0 + n) + (int64_t)(k0 + k) * g.ldb)
+                            : Bb;
+      cp_async16(RB + b_at(n, k), src, ok);
+    }
+    asm volatile("cp.async.commit_group;");
+  }
+};
+
+// floats at the start of shared memory shared by the main-loop slabs and the
+// resolve stages
+template <bool A_MC, bool B_KC>
+__host__ __device__ constexpr int resolve_region() {
+  return 2 * ResolveStager<A_MC, B_KC>::STAGE > 2 * TB_K * (TB_M + TB_N)
+             ? 2 * ResolveStager<A_MC, B_KC>::STAGE
+             : 2 * TB_K * (TB_M + TB_N);
+}
+
+// Output coordinates.  Warp w covers rows 64*(w & 1) + [0, 64) and columns
+// 16*(w >> 1) + [0, 16); lane l = (lx = l & 7, ly = l >> 3).  Fragment loads
+// of the 8 lx lanes are consecutive 16-byte chunks (one 128-byte line).
+__device__ __forceinline__ int row_of(int warp, int lane, int i) {
+  return 64 * (warp & 1) + 2 * (lane & 7) + (i & 1) + 16 * (i >> 1);
+}
+__device__ __forceinline__ int col_of(int warp, int lane, int j) {
+  return 16 * (warp >> 1) + 2 * (lane >> 3) + (j & 1) + 8 * (j >> 1);
+}
 
 template <int ALG, bool ARGMAX, bool A_MC, bool B_KC>
 __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
   if (fast_path_ruled_out(*g.gate, ALG)) return;
   extern __shared__ __align__(16) unsigned char smem[];
-  float* As0 = (float*)smem;              // 2 x [TB_K][TB_M]
-  float* Bs0 = As0 + 2 * TB_K * TB_M;     // 2 x [TB_K][TB_N]
-  float* vals = Bs0 + 2 * TB_K * TB_N;    // [NE][NT] final values (ARGMAX)
-  uint32_t* stage = (uint32_t*)(vals + NE * NT);  // [8 warps][2 * 32] resolve items
+  float* As0 = (float*)smem;           // 2 x TB_K*TB_M floats
+  float* Bs0 = As0 + 2 * TB_K * TB_M;  // 2 x TB_K*TB_N floats
+  float* vals = (float*)smem + resolve_region<A_MC, B_KC>();  // [NE][NT] (ARGMAX)
+  uint32_t* stage = (uint32_t*)(vals + NE * NT);              // [8 warps][64] items
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int tx = (warp & 1) * 8 + (lane & 7), ty = (warp >> 1) * 4 + (lane >> 3);
   const int m0 = blockIdx.x * TB_M, n0 = blockIdx.y * TB_N;
   const int bt = blockIdx.z;
   const float* Ab = g.A + bt * g.sab;
   const float* Bb = g.B + bt * g.sbb;
-  // per-slab "improved" bitmasks of this CTA: [T][NT]
   uint32_t* masks = g.ws + ((size_t)(bt * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) *
                                (size_t)g.T * NT;
+  const int r0 = row_of(warp, lane, 0), c0 = col_of(warp, lane, 0);
 
   float acc[8][4];
   const float z = Semi<ALG, float>::zero();
@@ -184,17 +297,31 @@ __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) before[i][j] = acc[i][j];
     }
-#pragma unroll 8
-    for (int kk = 0; kk < TB_K; ++kk) {
-      const float4 a0 = *(const float4*)(As + kk * TB_M + 4 * tx);
-      const float4 a1 = *(const float4*)(As + kk * TB_M + 64 + 4 * tx);
-      const float4 b0 = *(const float4*)(Bs + kk * TB_N + 4 * ty);
-      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float b[4] = {b0.x, b0.y, b0.z, b0.w};
+#pragma unroll 4
+    for (int kp = 0; kp < TB_K / 2; ++kp) {
+      const float* arow = As + kp * TB_M * 2 + 2 * r0;
+      const float* brow = Bs + kp * TB_N * 2 + 2 * c0;
+      unsigned long long a[8], b[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const ulonglong2 v = *(const ulonglong2*)(arow + 32 * q);
+        a[2 * q] = v.x;
+        a[2 * q + 1] = v.y;
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const ulonglong2 v = *(const ulonglong2*)(brow + 16 * q);
+        b[2 * q] = v.x;
+        b[2 * q + 1] = v.y;
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = tfold<ALG>(acc[i][j], tmul<ALG>(a[i], b[j]));
+        for (int j = 0; j < 4; ++j) {
+          float lo, hi;
+          unpack(tmul2<ALG>(a[i], b[j]), lo, hi);
+          acc[i][j] = tfold3<ALG>(acc[i][j], lo, hi);
+        }
     }
     if (ARGMAX) {
       uint32_t bits = 0;
@@ -220,29 +347,38 @@ __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
     // Resolve pass, last slab first: the deciding slab of an output is the
     // last one whose bit is set.  Items of a slab are compacted across the
     // warp so every lane scans at most one output per round.
-    if (g.T > 0) st.load(g, Ab, Bb, m0, n0, (g.T - 1) * TB_K, tid);
+    using RS = ResolveStager<A_MC, B_KC>;
+    RS rs;
+    auto stA = [&](int q) { return (float*)smem + q * RS::STAGE; };
+    auto stB = [&](int q) { return (float*)smem + q * RS::STAGE + RS::A_FLOATS; };
+    rs.issue(g, Ab, Bb, m0, n0, g.T - 1, stA(0), stB(0), tid);
+    uint32_t mask_next = masks[(size_t)(g.T - 1) * NT + tid];
     for (int t = g.T - 1; t >= 0; --t) {
-      const int buf = t & 1;
-      float* As = As0 + buf * TB_K * TB_M;
-      float* Bs = Bs0 + buf * TB_K * TB_N;
-      st.store(As, Bs, tid);
-      if (t > 0) st.load(g, Ab, Bb, m0, n0, (t - 1) * TB_K, tid);
+      const int s = (g.T - 1 - t) & 1;
+      const float* RA = stA(s);
+      const float* RB = stB(s);
+      const uint32_t mine = mask_next & remaining;
+      if (t >= 1) {
+        rs.issue(g, Ab, Bb, m0, n0, t - 1, stA(s ^ 1), stB(s ^ 1), tid);
+        mask_next = masks[(size_t)(t - 1) * NT + tid];
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
       __syncthreads();
-      uint32_t mine = masks[(size_t)t * NT + tid] & remaining;
       remaining &= ~mine;
-      int cnt = __popc(mine);
+      const int cnt = __popc(mine);
       int pos = cnt;  // inclusive warp scan
 #pragma unroll
       for (int d = 1; d < 32; d <<= 1) {
-        int v = __shfl_up_sync(0xffffffffu, pos, d);
+        const int v = __shfl_up_sync(0xffffffffu, pos, d);
         if (lane >= d) pos += v;
       }
       const int total = __shfl_sync(0xffffffffu, pos, 31);
-      int wr = pos - cnt;
+      const int kmax = min(TB_K, g.K - t * TB_K);
       for (int done = 0; done < total; done += 64) {
-        // write this lane's items that fall in [done, done + 64)
         uint32_t rest = mine;
-        int p = wr;
+        int p = pos - cnt;
         while (rest) {
           const int e = __ffs(rest) - 1;
           rest &= rest - 1;
@@ -250,18 +386,17 @@ __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
           ++p;
         }
         __syncwarp();
-        for (int q = lane; q < min(64, total - done); q += 32) {
+        const int here = min(64, total - done);
+        for (int q = lane; q < here; q += 32) {
           const uint32_t it = items[q];
           const int src = (int)(it >> 5), e = (int)(it & 31);
-          const int stx = (warp & 1) * 8 + (src & 7), sty = (warp >> 1) * 4 + (src >> 3);
-          const int mi = row_of(stx, e >> 2), nj = 4 * sty + (e & 3);
+          const int mi = row_of(warp, src, e >> 2), nj = col_of(warp, src, e & 3);
           const float v = vals[e * NT + warp * 32 + src];
           int kb = 0;
-          for (int kk = 0; kk < TB_K; ++kk) {
-            if (tmul<ALG>(As[kk * TB_M + mi], Bs[kk * TB_N + nj]) == v) {
-              kb = kk;
-              break;
-            }
+#pragma unroll
+          for (int kk = TB_K - 1; kk >= 0; --kk) {
+            const float pr = tmul<ALG>(RA[RS::a_at(mi, kk)], RB[RS::b_at(nj, kk)]);
+            if (kk < kmax && pr == v) kb = kk;
           }
           const int m = m0 + mi, n = n0 + nj;
           if (m < g.M && n < g.N)
@@ -277,19 +412,19 @@ __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
   for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int m = m0 + row_of(tx, i), n = n0 + 4 * ty + j;
+      const int m = m0 + row_of(warp, lane, i), n = n0 + col_of(warp, lane, j);
       if (m < g.M && n < g.N) {
         const int64_t off = cbase + (int64_t)m * g.scm + (int64_t)n * g.scn;
         float v = acc[i][j];
         if (ALG == OM_MAXMUL && v == 0.f) v = 0.f;  // zero() is +0; a -0 product never wins
         g.C[off] = v;
-        if (ARGMAX && (remaining >> (i * 4 + j)) & 1u) g.argmax[off] = 0u;
+        if (ARGMAX && ((remaining >> (i * 4 + j)) & 1u)) g.argmax[off] = 0u;
       }
     }
 }
 
 // ---------------------------------------------------------------------------
-// special-value scan over the affine operand views
+// special-value scan over the operands
 // ---------------------------------------------------------------------------
 // An operand of the fast path is `lines` runs of `inner` unit-stride floats
 // (inner % 4 == 0, 16-byte aligned), run l starting at (l % outer) * ld +
@@ -318,10 +453,9 @@ __global__ void special_scan_kernel(ScanArgs s0, ScanArgs s1, uint32_t* flags) {
     const ScanArgs& s = w ? s1 : s0;
     const int vec = s.inner / 4;
     for (int64_t l = blockIdx.x; l < s.lines; l += gridDim.x) {
-      const float4* run =
-          (const float4*)(s.p + (l % s.outer) * s.ld + (l / s.outer) * s.bs);
+      const float4* run = (const float4*)(s.p + (l % s.outer) * s.ld + (l / s.outer) * s.bs);
       for (int v = threadIdx.x; v < vec; v += blockDim.x) {
-        float4 x = run[v];
+        const float4 x = run[v];
         f |= classify_bits(__float_as_uint(x.x), s.pinf_bit, s.ninf_bit) |
              classify_bits(__float_as_uint(x.y), s.pinf_bit, s.ninf_bit) |
              classify_bits(__float_as_uint(x.z), s.pinf_bit, s.ninf_bit) |
@@ -335,8 +469,9 @@ __global__ void special_scan_kernel(ScanArgs s0, ScanArgs s1, uint32_t* flags) {
 
 template <int ALG, bool ARGMAX, bool A_MC, bool B_KC>
 int launch_fast(om_backend* be, const FastArgs& fa, int64_t batch) {
-  size_t smem = sizeof(float) * 2 * TB_K * (TB_M + TB_N) +
-                (ARGMAX ? NE * NT * sizeof(float) + 8 * 64 * sizeof(uint32_t) : 0);
+  const size_t smem =
+      ARGMAX ? sizeof(float) * (resolve_region<A_MC, B_KC>() + NE * NT) + 8 * 64 * sizeof(uint32_t)
+             : sizeof(float) * 2 * TB_K * (TB_M + TB_N);
   auto kern = tropical_fast_kernel<ALG, ARGMAX, A_MC, B_KC>;
   OM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
           "cudaFuncSetAttribute");
@@ -349,7 +484,7 @@ int launch_fast(om_backend* be, const FastArgs& fa, int64_t batch) {
 
 template <int ALG>
 int launch_fast_alg(om_backend* be, const FastArgs& fa, int64_t batch, bool amc, bool bkc) {
-  bool am = fa.argmax != nullptr;
+  const bool am = fa.argmax != nullptr;
 #define OM_FAST_CASE(X, Y, Z) \
   if (am == X && amc == Y && bkc == Z) return launch_fast<ALG, X, Y, Z>(be, fa, batch);
   OM_FAST_CASE(true, true, true)
@@ -378,8 +513,7 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
   *handled = false;
   if (g.dtype != OM_F32 || g.alg == OM_STANDARD) return OM_OK;
   if (g.M < 64 || g.N < 64 || g.K < 32) return OM_OK;
-  if (g.M > (1 << 30) || g.N > (1 << 30) || g.batch > 65535) return OM_OK;
-  if (g.K > (1 << 30)) return OM_OK;
+  if (g.M > (1 << 30) || g.N > (1 << 30) || g.K > (1 << 30) || g.batch > 65535) return OM_OK;
   bool amc, bkc;
   int64_t lda, ldb;
   if (g.sam == 1 && g.sak % 4 == 0 && g.M % 4 == 0) {
@@ -421,7 +555,7 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
   sb.lines = (int64_t)sb.outer * g.batch;
   sb.pinf_bit = SV_B_PINF;
   sb.ninf_bit = SV_B_NINF;
-  int blocks = (int)std::min<int64_t>(std::max(sa.lines, sb.lines), (int64_t)be->num_sms * 8);
+  const int blocks = (int)std::min<int64_t>(std::max(sa.lines, sb.lines), (int64_t)be->num_sms * 8);
   {
     ProfScope prof(be, "special_scan");
     special_scan_kernel<<<std::max(blocks, 1), 128, 0, be->stream>>>(sa, sb, be->d_flags);
