@@ -47,8 +47,8 @@ FP32_PEAK_TOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 # (profiles/tropical_instruction_mix.md).
 PAIR_CEILING_TOPS = 148 * 39 * 4 * 1.965e9 / 1e12
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
-# kernel, from the ncu capture summarised in profiles/ (None until captured).
-NCU_TRAFFIC_BYTES = None
+# kernel, from the ncu capture summarised in profiles/.
+NCU_TRAFFIC_BYTES = 34874880 + 21393408  # profiles/tropical_fast_maxplus_2048_ncu.md
 
 
 def load_pkg():
