@@ -137,6 +137,30 @@ int om_b200_profile_enable(om_backend* be, int on);
 int om_b200_profile_query(om_backend* be, int index, char* name, size_t len, double* total_ms,
                           int64_t* launches);
 
+/* Allocation-free tropical matrix product with argmax.  No counterpart in the
+ * reference: it exists for callers that must not allocate device memory
+ * while they run (a host that hands all device memory out of its own arena,
+ * a latency-critical path where an allocation could block or fail, an
+ * embedder that forbids library-owned allocations).
+ *
+ * C = A (x) B in MaxPlus / MinPlus / MaxMul f32, with the u32 argmax of the
+ * first winning k (same results as om_b200_contract with modes
+ * 'ij,jk->ik').  A (m x k, leading dimension lda), B (k x n, ldb), C and
+ * argmax (m x n, ldc) are column-major device buffers owned by the caller;
+ * work is issued on `stream` (a cudaStream_t; NULL = legacy default stream)
+ * and no om_backend is needed.  Nothing is allocated: the kernel's scratch
+ * lives in fixed device arrays of the library (32 MiB + 64 bytes, held on
+ * every GPU that loads the library until the process exits), which limits
+ * ceil(m/128) * ceil(n/64) * ceil(k/32) to 32768; larger problems on the
+ * fast path fail with OM_ERR_INVALID (use om_b200_contract for them).
+ * The first call on a device looks up the arrays' device addresses; make
+ * that first call before any stream capture.  All calls share the arrays,
+ * so calls that overlap on the GPU (other streams, other threads) race:
+ * serialise them. */
+int om_b200_tropical_matmul_argmax_noalloc(void* stream, om_algebra alg, int64_t m, int64_t n,
+                                           int64_t k, const float* a, int64_t lda, const float* b,
+                                           int64_t ldb, float* c, int64_t ldc, uint32_t* argmax);
+
 #ifdef __cplusplus
 }
 #endif

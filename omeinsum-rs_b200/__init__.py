@@ -36,6 +36,7 @@ EXPORTS = [
     "om_b200_sync", "om_b200_alloc", "om_b200_free", "om_b200_upload", "om_b200_download",
     "om_b200_copy_strided", "om_b200_contract", "om_b200_unary", "om_b200_tropical_backward",
     "om_b200_launch_count", "om_b200_profile_enable", "om_b200_profile_query",
+    "om_b200_tropical_matmul_argmax_noalloc",
 ]
 
 
@@ -83,6 +84,8 @@ def lib():
         L.om_b200_profile_query.argtypes = [P, I, ctypes.c_char_p, SZ,
                                             ctypes.POINTER(ctypes.c_double),
                                             ctypes.POINTER(ctypes.c_int64)]
+        L.om_b200_tropical_matmul_argmax_noalloc.argtypes = [P, I, I64, I64, I64, P, I64, P, I64,
+                                                             P, I64, P]
         _lib = L
     return _lib
 

@@ -601,3 +601,165 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
 }
 
 }  // namespace om
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the fast tropical GEMM with argmax.
+//
+// Some callers cannot allocate device memory while they run: code inside a
+// host that owns all device memory through its own arena, real-time paths
+// where a cudaMalloc / cudaMallocAsync could block or fail, and embedders that
+// forbid the library any allocation of its own.  For them this entry point
+// takes a caller's stream and plain column-major matrices and keeps the
+// argmax kernel's scratch (per-slab improvement bitmasks, plus the flag word
+// of the special-value gate) in fixed file-scope device arrays instead of the
+// stream-ordered pool.  Every GPU that loads the library holds these arrays
+// (32 MiB + 64 bytes) until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace om {
+namespace {
+
+constexpr size_t kNoAllocMaskWords = (32u << 20) / sizeof(uint32_t);  // 32 MiB of masks
+static __device__ __align__(256) uint32_t g_noalloc_masks[kNoAllocMaskWords];
+static __device__ __align__(256) uint32_t g_noalloc_flag[16];
+
+struct NoAllocSymbols {
+  bool ready = false;
+  uint32_t* masks = nullptr;
+  uint32_t* flag = nullptr;
+};
+
+// Device addresses of the two arrays, looked up once per device with that
+// device current (the host-side names are stand-ins, not device addresses).
+int noalloc_symbols(int device, NoAllocSymbols* out) {
+  static std::mutex mu;
+  static NoAllocSymbols table[64];
+  if (device < 0 || device >= 64) return set_error(OM_ERR_INVALID, "noalloc: device ordinal >= 64");
+  std::lock_guard<std::mutex> lock(mu);
+  NoAllocSymbols& s = table[device];
+  if (!s.ready) {
+    OM_CUDA(cudaGetSymbolAddress((void**)&s.masks, g_noalloc_masks),
+            "cudaGetSymbolAddress(noalloc masks)");
+    OM_CUDA(cudaGetSymbolAddress((void**)&s.flag, g_noalloc_flag),
+            "cudaGetSymbolAddress(noalloc flag)");
+    s.ready = true;
+  }
+  *out = s;
+  return OM_OK;
+}
+
+}  // namespace
+}  // namespace om
+
+extern "C" int om_b200_tropical_matmul_argmax_noalloc(void* stream, om_algebra alg, int64_t m,
+                                                      int64_t n, int64_t k, const float* a,
+                                                      int64_t lda, const float* b, int64_t ldb,
+                                                      float* c, int64_t ldc, uint32_t* argmax) {
+  using namespace om;
+  if (!a || !b || !c || !argmax)
+    return set_error(OM_ERR_INVALID, "om_b200_tropical_matmul_argmax_noalloc: null pointer");
+  if (alg != OM_MAXPLUS && alg != OM_MINPLUS && alg != OM_MAXMUL)
+    return set_error(OM_ERR_UNSUPPORTED,
+                     "om_b200_tropical_matmul_argmax_noalloc: algebra must be MaxPlus, MinPlus or MaxMul");
+  if (m < 0 || n < 0 || k < 1 || lda < std::max<int64_t>(m, 1) || ldb < k || ldc < std::max<int64_t>(m, 1))
+    return set_error(OM_ERR_INVALID,
+                     "om_b200_tropical_matmul_argmax_noalloc: bad sizes or leading dimensions");
+  if (m == 0 || n == 0) return OM_OK;
+  int device = 0;
+  OM_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+  NoAllocSymbols sym;
+  OM_TRY(noalloc_symbols(device, &sym));
+
+  // a backend view over the caller's stream; it owns nothing
+  om_backend view;
+  view.device = device;
+  view.stream = (cudaStream_t)stream;
+  OM_CUDA(cudaDeviceGetAttribute(&view.num_sms, cudaDevAttrMultiProcessorCount, device),
+          "cudaDeviceGetAttribute");
+  view.d_flags = sym.flag;
+
+  GemmArgs g{};
+  g.alg = alg;
+  g.dtype = OM_F32;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.batch = 1;
+  g.A = a;
+  g.sam = 1;
+  g.sak = lda;
+  g.B = b;
+  g.sbk = 1;
+  g.sbn = ldb;
+  g.C = c;
+  g.scm = 1;
+  g.scn = ldc;
+  g.argmax = argmax;
+
+  const bool fast = m >= 64 && n >= 64 && k >= 32 && m <= (1 << 30) && n <= (1 << 30) &&
+                    k <= (1 << 30) && m % 4 == 0 && k % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 &&
+                    aligned16(a) && aligned16(b);
+  if (!fast) return launch_gemm_exact(&view, g);  // no scratch on this path
+
+  const int64_t gx = (m + TB_M - 1) / TB_M, gy = (n + TB_N - 1) / TB_N, T = (k + TB_K - 1) / TB_K;
+  const int64_t words = gx * gy * T * NT;
+  if (words > (int64_t)kNoAllocMaskWords)
+    return set_error(OM_ERR_INVALID,
+                     "om_b200_tropical_matmul_argmax_noalloc: ceil(m/128)*ceil(n/64)*ceil(k/32) = " +
+                         std::to_string(gx * gy * T) + " exceeds the static workspace limit of " +
+                         std::to_string(kNoAllocMaskWords / NT) +
+                         " (32 MiB); use om_b200_contract for larger problems");
+
+  // the gate flag must start at zero on every call; the masks need no
+  // clearing (each is written before it is read)
+  OM_CUDA(cudaMemsetAsync(sym.flag, 0, sizeof(uint32_t), view.stream), "noalloc flag reset");
+  ScanArgs sa, sb;
+  sa.p = a;
+  sa.inner = (int)m;
+  sa.outer = (int)k;
+  sa.ld = lda;
+  sa.bs = 0;
+  sa.lines = k;
+  sa.pinf_bit = SV_A_PINF;
+  sa.ninf_bit = SV_A_NINF;
+  sb.p = b;
+  sb.inner = (int)k;
+  sb.outer = (int)n;
+  sb.ld = ldb;
+  sb.bs = 0;
+  sb.lines = n;
+  sb.pinf_bit = SV_B_PINF;
+  sb.ninf_bit = SV_B_NINF;
+  const int blocks = (int)std::min<int64_t>(std::max(k, n), (int64_t)view.num_sms * 8);
+  special_scan_kernel<<<std::max(blocks, 1), 128, 0, view.stream>>>(sa, sb, sym.flag);
+  note_launch();
+  OM_CUDA(cudaGetLastError(), "noalloc special_scan launch");
+
+  FastArgs fa;
+  fa.M = (int)m;
+  fa.N = (int)n;
+  fa.K = (int)k;
+  fa.T = (int)T;
+  fa.A = a;
+  fa.lda = lda;
+  fa.sab = 0;
+  fa.B = b;
+  fa.ldb = ldb;
+  fa.sbb = 0;
+  fa.C = c;
+  fa.scm = 1;
+  fa.scn = ldc;
+  fa.scb = 0;
+  fa.argmax = argmax;
+  fa.gate = sym.flag;
+  fa.ws = sym.masks;
+  switch (alg) {
+    case OM_MAXPLUS: OM_TRY((launch_fast<OM_MAXPLUS, true, true, true>(&view, fa, 1))); break;
+    case OM_MINPLUS: OM_TRY((launch_fast<OM_MINPLUS, true, true, true>(&view, fa, 1))); break;
+    default: OM_TRY((launch_fast<OM_MAXMUL, true, true, true>(&view, fa, 1))); break;
+  }
+  GemmArgs gated = g;
+  gated.fast_gate = sym.flag;
+  return launch_gemm_exact(&view, gated);
+}
