@@ -137,6 +137,45 @@ int om_b200_profile_enable(om_backend* be, int on);
 int om_b200_profile_query(om_backend* be, int index, char* name, size_t len, double* total_ms,
                           int64_t* launches);
 
+/* ---- einsum engine over a contraction tree --------------------------------
+ * Restates Einsum::execute / execute_with_argmax and the gradient tape of
+ * cost_and_gradient (src/einsum/engine.rs:125-301,392-578;
+ * src/einsum/backward.rs:405-799) on the device.
+ *
+ * Inputs: `ntensors` device tensors; tensor t has rank ndims[t], and its
+ * shape, strides and labels are the next ndims[t] entries of shapes / strides
+ * / ixs (concatenated over t).  Labels are int32 >= 0; size_labels[q] has
+ * extent size_values[q] (the size dictionary).  iy (length niy) are the
+ * output labels.
+ *
+ * Tree: `nnodes` binary nodes in post order.  Node i contracts children
+ * children[2i], children[2i+1]; a child value c < ntensors is leaf tensor c,
+ * c >= ntensors is node c - ntensors.  Its output labels are
+ * node_iy[node_iy_off[i] .. node_iy_off[i+1]).  The last node is the root.
+ * nnodes == 0 means the tree is the single leaf 0 (a unary einsum).
+ *
+ * Operands are normalised before each node (labels in neither the other
+ * operand nor the node output are reduced first, repeated labels take the
+ * diagonal), and the root is reduced / permuted to iy at the end.  `out`
+ * receives prod(extent of iy) contiguous column-major elements.
+ *
+ * With tape_out non-NULL the forward keeps a gradient tape (argmax of every
+ * node for the tropical algebras, every intermediate for Standard); pass it
+ * to om_b200_einsum_backward, then free it with om_b200_tape_free. */
+typedef struct om_tape om_tape;
+int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, int ntensors,
+                   const void* const* tensors, const int32_t* ndims, const int64_t* shapes,
+                   const int64_t* strides, const int32_t* ixs, int niy, const int32_t* iy,
+                   int nsizes, const int32_t* size_labels, const int64_t* size_values,
+                   int nnodes, const int32_t* children, const int32_t* node_iy_off,
+                   const int32_t* node_iy, void* out, om_tape** tape_out);
+
+/* GradientTape::backward (backward.rs:498-506, 678-728): given dy (shaped
+ * like the output, contiguous), writes the gradient of every input tensor t,
+ * contiguous column-major in the input's shape, to grads[t]. */
+int om_b200_einsum_backward(om_tape* tape, const void* dy, void* const* grads);
+int om_b200_tape_free(om_tape* tape);
+
 /* Allocation-free tropical matrix product with argmax.  No counterpart in the
  * reference: it exists for callers that must not allocate device memory
  * while they run (a host that hands all device memory out of its own arena,

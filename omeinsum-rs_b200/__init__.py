@@ -36,7 +36,8 @@ EXPORTS = [
     "om_b200_sync", "om_b200_alloc", "om_b200_free", "om_b200_upload", "om_b200_download",
     "om_b200_copy_strided", "om_b200_contract", "om_b200_unary", "om_b200_tropical_backward",
     "om_b200_launch_count", "om_b200_profile_enable", "om_b200_profile_query",
-    "om_b200_tropical_matmul_argmax_noalloc",
+    "om_b200_tropical_matmul_argmax_noalloc", "om_b200_einsum", "om_b200_einsum_backward",
+    "om_b200_tape_free",
 ]
 
 

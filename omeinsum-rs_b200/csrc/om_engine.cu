@@ -1,0 +1,370 @@
+// Einsum engine: contraction-tree walk, operand normalisation, gradient tape
+// and backward, all on the device through the library's own kernels.
+//
+// Restates the reference's engine (tensor4all/omeinsum-rs):
+//   tree walk            src/einsum/engine.rs:392-446 (execute_tree) and the
+//                        tape build of src/einsum/backward.rs:535-605
+//   normalisation        compute_normalized_binary_indices / normalize_binary_operand,
+//                        engine.rs:515-578; normalize_tape_operand, backward.rs:607-642
+//   root finalisation    finalize_tape_node, backward.rs:644-676; engine.rs:125-166
+//   backward             backprop_tape_node, backward.rs:678-728:
+//                        tropical binary -> argmax scatter (backward.rs:90-166),
+//                        tropical unary  -> tropical_unary_backward (:213-238),
+//                        Standard binary -> two contractions (:287-332),
+//                        Standard unary  -> index exchange (:183-195).
+// The forward follows the tape semantics in both modes: every binary node
+// writes its output in the node's label order, and the root is finalised to
+// iy.  Only the Standard value path of the reference (execute_tree) writes
+// intermediates in another order; values are the same.
+#include <algorithm>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "om_internal.h"
+#include "om_semiring.cuh"
+
+struct om_tape;
+
+namespace om {
+namespace {
+
+// device buffer freed on the backend's stream when the last owner goes
+std::shared_ptr<void> dev_alloc(om_backend* be, size_t bytes, int* rc) {
+  void* p = nullptr;
+  cudaError_t e = cudaMallocAsync(&p, bytes ? bytes : 16, be->stream);
+  if (e != cudaSuccess) {
+    *rc = check_cuda(e, "engine cudaMallocAsync");
+    return nullptr;
+  }
+  *rc = OM_OK;
+  cudaStream_t s = be->stream;
+  return std::shared_ptr<void>(p, [s](void* q) { cudaFreeAsync(q, s); });
+}
+
+struct DTensor {
+  std::shared_ptr<void> owner;  // null for caller-owned inputs
+  const void* ptr = nullptr;
+  std::vector<int64_t> shape, strides;
+  std::vector<int32_t> ix;
+  int64_t numel() const {
+    int64_t n = 1;
+    for (auto s : shape) n *= s;
+    return n;
+  }
+};
+
+std::vector<int64_t> col_strides(const std::vector<int64_t>& shape) {
+  std::vector<int64_t> st(shape.size());
+  int64_t s = 1;
+  for (size_t i = 0; i < shape.size(); ++i) {
+    st[i] = s;
+    s *= shape[i];
+  }
+  return st;
+}
+
+enum class Op { Leaf, Unary, Binary };
+
+struct TapeNode {
+  Op op;
+  DTensor content;
+  std::shared_ptr<void> argmax;  // u32, shaped like content (tropical)
+  int tensor_index = -1;         // Leaf
+  std::vector<int32_t> in_ix, out_ix;        // Unary
+  std::vector<int32_t> left_ix, right_ix;    // Binary (out_ix too)
+  int child0 = -1, child1 = -1;
+};
+
+template <typename T>
+__global__ void scatter_add_kernel(const T* __restrict__ dy, const uint32_t* __restrict__ am,
+                                   T* grad, int64_t n) {
+  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < n;
+       o += (int64_t)gridDim.x * blockDim.x)
+    atomicAdd(grad + am[o], dy[o]);
+}
+
+}  // namespace
+
+struct Engine {
+  om_backend* be;
+  om_algebra alg;
+  om_dtype dt;
+  size_t es;
+  bool tropical;
+  std::map<int32_t, int64_t> sizes;
+  std::vector<TapeNode> nodes;
+  std::vector<std::vector<int64_t>> input_shapes;
+  int root = -1;
+  bool keep;  // tape mode (argmax for tropical)
+
+  int64_t extent(int32_t l) const {
+    auto it = sizes.find(l);
+    return it == sizes.end() ? -1 : it->second;
+  }
+
+  int new_tensor(const std::vector<int32_t>& ix, DTensor& t) {
+    t.ix = ix;
+    t.shape.clear();
+    for (auto l : ix) {
+      int64_t e = extent(l);
+      if (e < 0) return set_error(OM_ERR_SHAPE, "einsum: label " + std::to_string(l) + " has no size");
+      t.shape.push_back(e);
+    }
+    t.strides = col_strides(t.shape);
+    int rc;
+    t.owner = dev_alloc(be, es * (size_t)std::max<int64_t>(t.numel(), 1), &rc);
+    t.ptr = t.owner.get();
+    return rc;
+  }
+
+  // execute_unary_naive / execute_unary_with_argmax into a new tensor
+  int unary(const DTensor& x, const std::vector<int32_t>& oix, bool with_argmax, DTensor& y,
+            std::shared_ptr<void>& am) {
+    OM_TRY(new_tensor(oix, y));
+    uint32_t* amp = nullptr;
+    if (with_argmax) {
+      int rc;
+      am = dev_alloc(be, 4 * (size_t)std::max<int64_t>(y.numel(), 1), &rc);
+      OM_TRY(rc);
+      amp = (uint32_t*)am.get();
+    }
+    return launch_unary(be, alg, dt, x.ptr, (int)x.ix.size(), x.ix.data(), x.shape.data(),
+                        x.strides.data(), (int)oix.size(), oix.data(), y.shape.data(),
+                        (void*)y.ptr, amp);
+  }
+
+  int contract(const DTensor& a, const std::vector<int32_t>& ia, const DTensor& b,
+               const std::vector<int32_t>& ib, const std::vector<int32_t>& iy, bool with_argmax,
+               DTensor& c, std::shared_ptr<void>& am) {
+    OM_TRY(new_tensor(iy, c));
+    uint32_t* amp = nullptr;
+    if (with_argmax) {
+      int rc;
+      am = dev_alloc(be, 4 * (size_t)std::max<int64_t>(c.numel(), 1), &rc);
+      OM_TRY(rc);
+      amp = (uint32_t*)am.get();
+    }
+    return om_b200_contract(be, alg, dt, a.ptr, (int)ia.size(), a.shape.data(), a.strides.data(),
+                            ia.data(), b.ptr, (int)ib.size(), b.shape.data(), b.strides.data(),
+                            ib.data(), (int)iy.size(), c.shape.data(), iy.data(), (void*)c.ptr, amp);
+  }
+
+  // compute_normalized_binary_indices (engine.rs:515-535)
+  static std::vector<int32_t> normalized(const std::vector<int32_t>& ix,
+                                         const std::vector<int32_t>& other,
+                                         const std::vector<int32_t>& out) {
+    std::vector<int32_t> r;
+    for (auto l : ix) {
+      bool keep = std::find(other.begin(), other.end(), l) != other.end() ||
+                  std::find(out.begin(), out.end(), l) != out.end();
+      if (keep && std::find(r.begin(), r.end(), l) == r.end()) r.push_back(l);
+    }
+    return r;
+  }
+
+  int push_unary(int child, const std::vector<int32_t>& oix, int* out_node) {
+    TapeNode n;
+    n.op = Op::Unary;
+    n.in_ix = nodes[child].content.ix;
+    n.out_ix = oix;
+    n.child0 = child;
+    OM_TRY(unary(nodes[child].content, oix, keep && tropical, n.content, n.argmax));
+    nodes.push_back(std::move(n));
+    *out_node = (int)nodes.size() - 1;
+    return OM_OK;
+  }
+
+  int normalize(int node, const std::vector<int32_t>& other, const std::vector<int32_t>& out,
+                int* out_node) {
+    auto nix = normalized(nodes[node].content.ix, other, out);
+    if (nix == nodes[node].content.ix) {
+      *out_node = node;
+      return OM_OK;
+    }
+    return push_unary(node, nix, out_node);
+  }
+
+  int backprop(int idx, const DTensor& dy, void* const* grads);
+};
+
+int Engine::backprop(int idx, const DTensor& dy, void* const* grads) {
+  TapeNode& n = nodes[idx];
+  if (n.op == Op::Leaf) {
+    // dy is contiguous in the leaf's own label order and shape
+    const int64_t cnt = dy.numel();
+    OM_CUDA(cudaMemcpyAsync(grads[n.tensor_index], dy.ptr, es * (size_t)cnt,
+                            cudaMemcpyDeviceToDevice, be->stream),
+            "einsum grad copy");
+    return OM_OK;
+  }
+  if (n.op == Op::Unary) {
+    const DTensor& child = nodes[n.child0].content;
+    DTensor g;
+    if (tropical) {
+      // tropical_unary_backward: zero tensor, grad[argmax[o]] += dy[o]
+      OM_TRY(new_tensor(child.ix, g));
+      OM_CUDA(cudaMemsetAsync((void*)g.ptr, 0, es * (size_t)g.numel(), be->stream), "memset");
+      const int64_t cnt = dy.numel();
+      int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((cnt + 255) / 256, (int64_t)be->num_sms * 16));
+      {
+        ProfScope prof(be, "unary_scatter");
+        if (dt == OM_F32)
+          scatter_add_kernel<float><<<blocks, 256, 0, be->stream>>>(
+              (const float*)dy.ptr, (const uint32_t*)n.argmax.get(), (float*)g.ptr, cnt);
+        else
+          scatter_add_kernel<double><<<blocks, 256, 0, be->stream>>>(
+              (const double*)dy.ptr, (const uint32_t*)n.argmax.get(), (double*)g.ptr, cnt);
+        note_launch();
+        OM_CUDA(cudaGetLastError(), "scatter launch");
+      }
+    } else {
+      // contract_unary_backward: index exchange out_ix -> in_ix
+      std::shared_ptr<void> none;
+      OM_TRY(unary(dy, n.in_ix, false, g, none));
+    }
+    g.ix = child.ix;
+    return backprop(n.child0, g, grads);
+  }
+  const DTensor& l = nodes[n.child0].content;
+  const DTensor& r = nodes[n.child1].content;
+  DTensor gl, gr;
+  if (tropical) {
+    OM_TRY(new_tensor(n.left_ix, gl));
+    OM_TRY(new_tensor(n.right_ix, gr));
+    OM_CUDA(cudaMemsetAsync((void*)gl.ptr, 0, es * (size_t)gl.numel(), be->stream), "memset");
+    OM_CUDA(cudaMemsetAsync((void*)gr.ptr, 0, es * (size_t)gr.numel(), be->stream), "memset");
+    OM_TRY(om_b200_tropical_backward(be, dt, dy.ptr, (const uint32_t*)n.argmax.get(),
+                                     (int)n.left_ix.size(), l.shape.data(), n.left_ix.data(),
+                                     (int)n.right_ix.size(), r.shape.data(), n.right_ix.data(),
+                                     (int)n.out_ix.size(), dy.shape.data(), n.out_ix.data(),
+                                     (void*)gl.ptr, (void*)gr.ptr));
+  } else {
+    // standard_backward: grad_a = dy (x) b -> ia, grad_b = a (x) dy -> ib
+    std::shared_ptr<void> none;
+    OM_TRY(contract(dy, n.out_ix, r, n.right_ix, n.left_ix, false, gl, none));
+    OM_TRY(contract(l, n.left_ix, dy, n.out_ix, n.right_ix, false, gr, none));
+  }
+  OM_TRY(backprop(n.child0, gl, grads));
+  return backprop(n.child1, gr, grads);
+}
+
+}  // namespace om
+
+struct om_tape {
+  om::Engine eng;
+};
+
+using namespace om;
+
+extern "C" int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, int ntensors,
+                              const void* const* tensors, const int32_t* ndims,
+                              const int64_t* shapes, const int64_t* strides, const int32_t* ixs,
+                              int niy, const int32_t* iy, int nsizes, const int32_t* size_labels,
+                              const int64_t* size_values, int nnodes, const int32_t* children,
+                              const int32_t* node_iy_off, const int32_t* node_iy, void* out,
+                              om_tape** tape_out) {
+  if (!be || !tensors || !ndims || !out || ntensors < 1 || niy < 0 || nnodes < 0 ||
+      (nnodes > 0 && (!children || !node_iy_off)))
+    return set_error(OM_ERR_INVALID, "om_b200_einsum: bad argument");
+  if (dtype != OM_F32 && dtype != OM_F64)
+    return set_error(OM_ERR_UNSUPPORTED, "om_b200_einsum: dtype must be f32 or f64");
+  if (nnodes == 0 && ntensors != 1)
+    return set_error(OM_ERR_INVALID, "om_b200_einsum: a tree without nodes needs exactly one tensor");
+  if (nnodes > 0 && nnodes != ntensors - 1)
+    return set_error(OM_ERR_INVALID, "om_b200_einsum: a binary tree over n tensors has n-1 nodes");
+  OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  auto* tape = new om_tape();
+  Engine& E = tape->eng;
+  E.be = be;
+  E.alg = alg;
+  E.dt = dtype;
+  E.es = dtype_size(dtype);
+  E.tropical = alg != OM_STANDARD;
+  E.keep = tape_out != nullptr;
+  for (int q = 0; q < nsizes; ++q) E.sizes[size_labels[q]] = size_values[q];
+  std::unique_ptr<om_tape> guard(tape);
+
+  // leaves
+  int64_t off = 0;
+  std::vector<int> leaf_node(ntensors);
+  for (int t = 0; t < ntensors; ++t) {
+    TapeNode n;
+    n.op = Op::Leaf;
+    n.tensor_index = t;
+    n.content.ptr = tensors[t];
+    n.content.shape.assign(shapes + off, shapes + off + ndims[t]);
+    n.content.strides.assign(strides + off, strides + off + ndims[t]);
+    n.content.ix.assign(ixs + off, ixs + off + ndims[t]);
+    for (int d = 0; d < ndims[t]; ++d) {
+      auto it = E.sizes.find(ixs[off + d]);
+      if (it == E.sizes.end()) E.sizes[ixs[off + d]] = shapes[off + d];
+      else if (it->second != shapes[off + d])
+        return set_error(OM_ERR_SHAPE, "om_b200_einsum: label " + std::to_string(ixs[off + d]) +
+                                           " has two extents");
+    }
+    E.input_shapes.push_back(n.content.shape);
+    off += ndims[t];
+    E.nodes.push_back(std::move(n));
+    leaf_node[t] = (int)E.nodes.size() - 1;
+  }
+  std::vector<int32_t> final_iy(iy, iy + niy);
+
+  int cur = leaf_node[0];
+  if (nnodes > 0) {
+    std::vector<int> node_of(nnodes, -1);
+    for (int i = 0; i < nnodes; ++i) {
+      auto resolve = [&](int c, int* out_node) -> int {
+        if (c < 0 || c >= ntensors + i)
+          return set_error(OM_ERR_INVALID, "om_b200_einsum: child refers to a later node");
+        *out_node = c < ntensors ? leaf_node[c] : node_of[c - ntensors];
+        return OM_OK;
+      };
+      int l, r;
+      OM_TRY(resolve(children[2 * i], &l));
+      OM_TRY(resolve(children[2 * i + 1], &r));
+      std::vector<int32_t> niy_(node_iy + node_iy_off[i], node_iy + node_iy_off[i + 1]);
+      const std::vector<int32_t> rix0 = E.nodes[r].content.ix;
+      OM_TRY(E.normalize(l, rix0, niy_, &l));
+      const std::vector<int32_t> lix = E.nodes[l].content.ix;
+      OM_TRY(E.normalize(r, lix, niy_, &r));
+      TapeNode n;
+      n.op = Op::Binary;
+      n.child0 = l;
+      n.child1 = r;
+      n.left_ix = lix;
+      n.right_ix = E.nodes[r].content.ix;
+      n.out_ix = niy_;
+      OM_TRY(E.contract(E.nodes[l].content, n.left_ix, E.nodes[r].content, n.right_ix, niy_,
+                        E.keep && E.tropical, n.content, n.argmax));
+      E.nodes.push_back(std::move(n));
+      node_of[i] = (int)E.nodes.size() - 1;
+    }
+    cur = node_of[nnodes - 1];
+  }
+  // finalise to iy (a leaf root is always passed through the unary einsum)
+  if (nnodes == 0 || E.nodes[cur].content.ix != final_iy) OM_TRY(E.push_unary(cur, final_iy, &cur));
+  E.root = cur;
+  const DTensor& res = E.nodes[cur].content;
+  OM_CUDA(cudaMemcpyAsync(out, res.ptr, E.es * (size_t)res.numel(), cudaMemcpyDeviceToDevice,
+                          be->stream),
+          "einsum result copy");
+  if (tape_out) *tape_out = guard.release();
+  return OM_OK;
+}
+
+extern "C" int om_b200_einsum_backward(om_tape* tape, const void* dy, void* const* grads) {
+  if (!tape || !dy || !grads) return set_error(OM_ERR_INVALID, "om_b200_einsum_backward: null argument");
+  Engine& E = tape->eng;
+  OM_CUDA(cudaSetDevice(E.be->device), "cudaSetDevice");
+  DTensor d = E.nodes[E.root].content;
+  d.owner.reset();
+  d.ptr = dy;
+  return E.backprop(E.root, d, grads);
+}
+
+extern "C" int om_b200_tape_free(om_tape* tape) {
+  delete tape;
+  return OM_OK;
+}

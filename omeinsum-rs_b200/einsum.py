@@ -1,0 +1,274 @@
+"""Einsum front end of the B200 backend: contraction trees, a greedy order,
+the engine call (om_b200_einsum) and its gradient (om_b200_einsum_backward).
+
+Mirrors the reference's `Einsum` (src/einsum/engine.rs:37-110):
+`Einsum(ixs, iy, size_dict)`, `optimize_greedy()`, `set_contraction_tree()`,
+`execute(algebra, tensors)`, and `cost_and_gradient` (backward.rs:769-799).
+Trees are nested pairs of leaf indices, e.g. ((0, 1), 2), each node carrying
+its output labels; they are encoded in post order for the C ABI.
+
+The greedy orderer replaces omeco's GreedyMethod (omeco 0.2.4 is not
+available here); both the oracle and the device take the same tree.
+"""
+from __future__ import annotations
+
+import ctypes
+import itertools
+
+import numpy as np
+
+from . import B200, DTYPES, Storage, _alg, _check, _i32, _i64, _p, lib
+
+
+def _bind():
+    L = lib()
+    if not getattr(L, "_einsum_bound", False):
+        P, I = ctypes.c_void_p, ctypes.c_int
+        L.om_b200_einsum.argtypes = [P, I, I, I, P, P, P, P, P, I, P, I, P, P, I, P, P, P, P,
+                                     ctypes.POINTER(P)]
+        L.om_b200_einsum_backward.argtypes = [P, P, P]
+        L.om_b200_tape_free.argtypes = [P]
+        L._einsum_bound = True
+    return L
+
+
+# ---------------------------------------------------------------------------
+# trees
+# ---------------------------------------------------------------------------
+def tree_output_labels(tree, ixs, iy):
+    """Labels of every node: those of its subtree that appear outside it or
+    in iy (what omeco's NestedEinsum stores per node)."""
+    from collections import Counter
+    total = Counter(l for ix in ixs for l in set(ix))
+    final = set(iy)
+
+    def leaves(t):
+        return [t] if isinstance(t, int) else leaves(t[0]) + leaves(t[1])
+
+    out = {}
+
+    def rec(t):
+        if isinstance(t, int):
+            return list(dict.fromkeys(ixs[t]))
+        a, b = rec(t[0]), rec(t[1])
+        inside = Counter(l for i in leaves(t) for l in set(ixs[i]))
+        labels = []
+        for l in a + b:
+            if l in labels:
+                continue
+            if l in final or inside[l] < total[l]:
+                labels.append(l)
+        out[id(t)] = labels
+        return labels
+
+    rec(tree)
+    return out
+
+
+def encode_tree(tree, ixs, iy):
+    """Post-order (children, node_iys) arrays for om_b200_einsum / the oracle."""
+    n = len(ixs)
+    labels = tree_output_labels(tree, ixs, iy)
+    children, node_iys = [], []
+
+    def rec(t):
+        if isinstance(t, int):
+            return t
+        a, b = rec(t[0]), rec(t[1])
+        children.extend([a, b])
+        node_iys.append(labels[id(t)])
+        return n + len(node_iys) - 1
+
+    rec(tree)
+    return children, node_iys
+
+
+def greedy_tree(ixs, iy, sizes):
+    """Greedy pairwise order: repeatedly contract the pair (sharing a label if
+    any does) that minimises size(out) - size(a) - size(b); ties go to the
+    lowest pair of positions.  Deterministic."""
+    from collections import Counter
+    final = set(iy)
+    items = [(i, list(dict.fromkeys(ix))) for i, ix in enumerate(ixs)]
+    count = Counter(l for _, ix in items for l in ix)
+
+    def size(labels):
+        s = 1
+        for l in labels:
+            s *= sizes[l]
+        return s
+
+    while len(items) > 1:
+        best = None
+        share_any = any(set(a[1]) & set(b[1]) for a, b in itertools.combinations(items, 2))
+        for (pa, a), (pb, b) in itertools.combinations(enumerate(items), 2):
+            if share_any and not (set(a[1]) & set(b[1])):
+                continue
+            both = Counter(a[1]) + Counter(b[1])
+            out = [l for l in dict.fromkeys(a[1] + b[1]) if l in final or count[l] > both[l]]
+            cost = size(out) - size(a[1]) - size(b[1])
+            if best is None or cost < best[0]:
+                best = (cost, pa, pb, out)
+        _, pa, pb, out = best
+        ta, tb = items[pa][0], items[pb][0]
+        for l in items[pa][1] + items[pb][1]:
+            count[l] -= 1
+        for l in out:
+            count[l] += 1
+        items = [it for k, it in enumerate(items) if k not in (pa, pb)] + [((ta, tb), out)]
+    return items[0][0]
+
+
+def tree_cost(tree, ixs, iy, sizes):
+    """(time complexity, space complexity) of a tree: sum over nodes of the
+    product of all label extents involved, and the largest intermediate."""
+    labels = tree_output_labels(tree, ixs, iy)
+    tc, sc = 0, 0
+
+    def rec(t):
+        nonlocal tc, sc
+        if isinstance(t, int):
+            return list(dict.fromkeys(ixs[t]))
+        a, b = rec(t[0]), rec(t[1])
+        allv = list(dict.fromkeys(a + b))
+        p = 1
+        for l in allv:
+            p *= sizes[l]
+        tc += p
+        o = 1
+        for l in labels[id(t)]:
+            o *= sizes[l]
+        sc = max(sc, o)
+        return labels[id(t)]
+
+    rec(tree)
+    return tc, sc
+
+
+# ---------------------------------------------------------------------------
+# engine calls
+# ---------------------------------------------------------------------------
+class Einsum:
+    """Einsum{ixs, iy, size_dict, optimized} (engine.rs:37-110)."""
+
+    def __init__(self, ixs, iy, size_dict):
+        self.ixs = [list(ix) for ix in ixs]
+        self.iy = list(iy)
+        self.size_dict = dict(size_dict)
+        self.tree = None
+
+    def optimize_greedy(self):
+        self.tree = greedy_tree(self.ixs, self.iy, self.size_dict) if len(self.ixs) > 1 else 0
+        return self
+
+    def set_contraction_tree(self, tree):
+        self.tree = tree
+        return self
+
+    def encoded(self):
+        if self.tree is None:
+            self.optimize_greedy()
+        if isinstance(self.tree, int):
+            return [], []
+        return encode_tree(self.tree, self.ixs, self.iy)
+
+    def _call(self, be: B200, alg, tensors, out, tape):
+        L = _bind()
+        children, node_iys = self.encoded()
+        dtype = tensors[0].dtype
+        ptrs = (ctypes.c_void_p * len(tensors))(*[t.ptr for t in tensors])
+        nd = _i32([len(ix) for ix in self.ixs])
+        shapes = _i64([self.size_dict[l] for ix in self.ixs for l in ix])
+        strides = _i64([s for ix in self.ixs for s in _col([self.size_dict[l] for l in ix])])
+        ixs = _i32([l for ix in self.ixs for l in ix])
+        iy = _i32(self.iy)
+        sl = _i32(list(self.size_dict.keys()))
+        sv = _i64(list(self.size_dict.values()))
+        ch = _i32(children)
+        off = _i32(np.cumsum([0] + [len(x) for x in node_iys]))
+        niy = _i32([l for x in node_iys for l in x])
+        _check(L.om_b200_einsum(be.h, _alg(alg), DTYPES[dtype], len(tensors), ptrs, _p(nd),
+                                _p(shapes), _p(strides), _p(ixs), len(iy), _p(iy), len(sl),
+                                _p(sl), _p(sv), len(node_iys), _p(ch), _p(off), _p(niy),
+                                out.ptr, tape))
+
+    def out_size(self):
+        return int(np.prod([self.size_dict[l] for l in self.iy])) if self.iy else 1
+
+    def execute(self, be: B200, alg, tensors):
+        """Einsum::execute (engine.rs:125-166); tensors are contiguous Storages."""
+        out = be.alloc(self.out_size(), tensors[0].dtype)
+        self._call(be, alg, tensors, out, None)
+        return out
+
+    def cost_and_gradient(self, be: B200, alg, tensors, dy=None):
+        """cost_and_gradient (backward.rs:769-799).  dy defaults to the
+        algebra's one() as in the reference (0 for MaxPlus/MinPlus, so pass
+        dy = [1] to recover a tropical configuration)."""
+        out = be.alloc(self.out_size(), tensors[0].dtype)
+        tape = ctypes.c_void_p()
+        self._call(be, alg, tensors, out, ctypes.byref(tape))
+        try:
+            if dy is None:
+                one = 1.0 if _alg(alg) in (0, 3) else 0.0
+                dy = np.full(self.out_size(), one, dtype=tensors[0].dtype)
+            d = dy if isinstance(dy, Storage) else be.from_slice(np.asarray(dy, tensors[0].dtype))
+            grads = [be.alloc(t.n, t.dtype) for t in tensors]
+            ptrs = (ctypes.c_void_p * len(grads))(*[g.ptr for g in grads])
+            _check(_bind().om_b200_einsum_backward(tape, d.ptr, ptrs))
+        finally:
+            _bind().om_b200_tape_free(tape)
+        return out, grads
+
+
+def _col(shape):
+    s, out = 1, []
+    for d in shape:
+        out.append(s)
+        s *= d
+    return out
+
+
+# ---------------------------------------------------------------------------
+# benchmark networks, seeded
+# ---------------------------------------------------------------------------
+def random_regular3(n: int, seed: int):
+    """Seeded 3-regular graph by stub matching with rejection (the method of
+    the reference's examples/profile_network.rs:75-106, with a seeded
+    generator instead of the thread RNG).  Edges (u < v), sorted."""
+    assert n % 2 == 0 and n >= 4
+    rng = np.random.default_rng(seed)
+    for _ in range(10000):
+        stubs = np.repeat(np.arange(n), 3)
+        rng.shuffle(stubs)
+        pairs = stubs.reshape(-1, 2)
+        if np.any(pairs[:, 0] == pairs[:, 1]):
+            continue
+        e = {(int(min(u, v)), int(max(u, v))) for u, v in pairs}
+        if len(e) == len(pairs):
+            return sorted(e)
+    raise RuntimeError("failed to generate a 3-regular graph")
+
+
+def mis_network(n: int, seed: int, dtype=np.float32):
+    """Maximum-independent-set tropical network (MaxPlus): vertex tensors
+    [0, 1] over label v, edge tensors [[0, 0], [0, -inf]] over (u, v)
+    (tests/suites/showcase.rs:1031-1173 construction), output scalar."""
+    edges = random_regular3(n, seed)
+    ixs = [[v] for v in range(n)] + [[u, v] for u, v in edges]
+    tensors = [np.array([0, 1], dtype)] * n + [np.array([0, 0, 0, -np.inf], dtype)] * len(edges)
+    return ixs, [], {v: 2 for v in range(n)}, tensors, edges
+
+
+def ising_network(n: int, seed: int, beta: float = 1.0):
+    """Ising spin-glass partition function (Standard f64): edge tensors
+    exp(beta*J*s_i*s_j), J ~ N(0,1), index 0 <-> s = +1; no vertex tensors."""
+    edges = random_regular3(n, seed)
+    rng = np.random.default_rng(seed + 1)
+    J = rng.standard_normal(len(edges))
+    tensors = []
+    for j in J:
+        t = np.exp(beta * j * np.array([[1.0, -1.0], [-1.0, 1.0]]))
+        tensors.append(np.asfortranarray(t).reshape(-1, order="F"))
+    ixs = [[u, v] for u, v in edges]
+    return ixs, [], {v: 2 for v in range(n)}, tensors, edges
