@@ -54,7 +54,7 @@ enum {
   OM_ERR_TIMEOUT = 7      /* a bounded wait ran out                              */
 };
 
-#define OM_MAX_DIMS 24
+#define OM_MAX_DIMS 64
 
 /* Backend::name (traits.rs:50) -- returns "b200". */
 const char* om_b200_name(void);

@@ -32,6 +32,7 @@ __global__ void tropical_scatter(const T* __restrict__ gc, const uint32_t* __res
                                  T* ga, T* gb, BwdDesc d, int64_t n) {
   for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < n;
        o += (int64_t)gridDim.x * blockDim.x) {
+    if (gc[o] == T(0)) continue;
     int64_t val[2 * OM_MAX_DIMS];
     int64_t rem = o;
     for (int k = 0; k < d.nc; ++k) {
@@ -47,8 +48,14 @@ __global__ void tropical_scatter(const T* __restrict__ gc, const uint32_t* __res
     for (int k = 0; k < d.na; ++k) pa += val[d.aslot[k]] * d.astride[k];
     for (int k = 0; k < d.nb; ++k) pb += val[d.bslot[k]] * d.bstride[k];
     T g = gc[o];
-    atomicAdd(ga + pa, g);
-    atomicAdd(gb + pb, g);
+    // adding an exact zero changes no sum, so zeros are skipped: the
+    // gradients of optimisation problems are one-hot and mostly zero, and
+    // their many zero contributions would otherwise contend for the same
+    // broadcast targets
+    if (g != T(0)) {
+      atomicAdd(ga + pa, g);
+      atomicAdd(gb + pb, g);
+    }
   }
 }
 
@@ -117,6 +124,7 @@ extern "C" int om_b200_tropical_backward(om_backend* be, om_dtype dtype, const v
   if ((int)slot.size() > 2 * OM_MAX_DIMS) return set_error(OM_ERR_INVALID, "too many labels");
   if (n == 0) return OM_OK;
   int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)be->num_sms * 32));
+  ProfScope prof(be, "tropical_scatter");
   if (dtype == OM_F32)
     tropical_scatter<float><<<blocks, 256, 0, be->stream>>>((const float*)grad_c, argmax,
                                                             (float*)grad_a, (float*)grad_b, d, n);

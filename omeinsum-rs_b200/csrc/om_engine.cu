@@ -12,10 +12,11 @@
 //                        tropical unary  -> tropical_unary_backward (:213-238),
 //                        Standard binary -> two contractions (:287-332),
 //                        Standard unary  -> index exchange (:183-195).
-// The forward follows the tape semantics in both modes: every binary node
-// writes its output in the node's label order, and the root is finalised to
-// iy.  Only the Standard value path of the reference (execute_tree) writes
-// intermediates in another order; values are the same.
+// Every binary node writes its output in native order (free labels of the
+// left operand, free labels of the right one, batch labels), as the
+// reference's value path does (contract_binary_native_order, ops.rs:122-143),
+// so the GEMM writes without a permutation; the root is finalised to iy.  The
+// tape keys every gradient by label, so this order changes no result.
 #include <algorithm>
 #include <map>
 #include <memory>
@@ -82,7 +83,7 @@ __global__ void scatter_add_kernel(const T* __restrict__ dy, const uint32_t* __r
                                    T* grad, int64_t n) {
   for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < n;
        o += (int64_t)gridDim.x * blockDim.x)
-    atomicAdd(grad + am[o], dy[o]);
+    if (dy[o] != T(0)) atomicAdd(grad + am[o], dy[o]);  // zeros change no sum
 }
 
 }  // namespace
@@ -162,6 +163,26 @@ struct Engine {
       if (keep && std::find(r.begin(), r.end(), l) == r.end()) r.push_back(l);
     }
     return r;
+  }
+
+  // native_binary_output_indices (src/tensor/ops.rs:12-35): free labels of
+  // A, then free labels of B, then batch labels -- the order the GEMM writes
+  // without a permutation; falls back to the node's own order if that does
+  // not cover it
+  static std::vector<int32_t> native_order(const std::vector<int32_t>& ia,
+                                           const std::vector<int32_t>& ib,
+                                           const std::vector<int32_t>& iy) {
+    auto has = [](const std::vector<int32_t>& v, int32_t l) {
+      return std::find(v.begin(), v.end(), l) != v.end();
+    };
+    std::vector<int32_t> r;
+    for (auto l : ia)
+      if (has(iy, l) && !has(ib, l) && !has(r, l)) r.push_back(l);
+    for (auto l : ib)
+      if (has(iy, l) && !has(ia, l) && !has(r, l)) r.push_back(l);
+    for (auto l : ia)
+      if (has(iy, l) && has(ib, l) && !has(r, l)) r.push_back(l);
+    return r.size() == iy.size() ? r : iy;
   }
 
   int push_unary(int child, const std::vector<int32_t>& oix, int* out_node) {
@@ -335,8 +356,8 @@ extern "C" int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, in
       n.child1 = r;
       n.left_ix = lix;
       n.right_ix = E.nodes[r].content.ix;
-      n.out_ix = niy_;
-      OM_TRY(E.contract(E.nodes[l].content, n.left_ix, E.nodes[r].content, n.right_ix, niy_,
+      n.out_ix = Engine::native_order(n.left_ix, n.right_ix, niy_);
+      OM_TRY(E.contract(E.nodes[l].content, n.left_ix, E.nodes[r].content, n.right_ix, n.out_ix,
                         E.keep && E.tropical, n.content, n.argmax));
       E.nodes.push_back(std::move(n));
       node_of[i] = (int)E.nodes.size() - 1;

@@ -37,29 +37,20 @@ def _bind():
 # ---------------------------------------------------------------------------
 def tree_output_labels(tree, ixs, iy):
     """Labels of every node: those of its subtree that appear outside it or
-    in iy (what omeco's NestedEinsum stores per node)."""
+    in iy (what omeco's NestedEinsum stores per node), keyed by id(node)."""
     from collections import Counter
     total = Counter(l for ix in ixs for l in set(ix))
     final = set(iy)
-
-    def leaves(t):
-        return [t] if isinstance(t, int) else leaves(t[0]) + leaves(t[1])
-
     out = {}
 
     def rec(t):
         if isinstance(t, int):
-            return list(dict.fromkeys(ixs[t]))
-        a, b = rec(t[0]), rec(t[1])
-        inside = Counter(l for i in leaves(t) for l in set(ixs[i]))
-        labels = []
-        for l in a + b:
-            if l in labels:
-                continue
-            if l in final or inside[l] < total[l]:
-                labels.append(l)
+            return list(dict.fromkeys(ixs[t])), Counter(set(ixs[t]))
+        (a, ca), (b, cb) = rec(t[0]), rec(t[1])
+        inside = ca + cb
+        labels = [l for l in dict.fromkeys(a + b) if l in final or inside[l] < total[l]]
         out[id(t)] = labels
-        return labels
+        return labels, inside
 
     rec(tree)
     return out
@@ -163,24 +154,38 @@ class Einsum:
 
     def set_contraction_tree(self, tree):
         self.tree = tree
+        self._enc = None
+        return self
+
+    def set_encoded(self, children, node_iys):
+        """Use an already encoded tree (post-order children and node labels)."""
+        self._enc = (list(children), [list(x) for x in node_iys])
         return self
 
     def encoded(self):
+        if getattr(self, "_enc", None) is not None:
+            return self._enc
         if self.tree is None:
             self.optimize_greedy()
         if isinstance(self.tree, int):
             return [], []
         return encode_tree(self.tree, self.ixs, self.iy)
 
-    def _call(self, be: B200, alg, tensors, out, tape):
+    def _call(self, be: B200, alg, tensors, out, tape, views=None):
+        """views (optional): per tensor (element offset, shape, strides,
+        labels) of a strided view into the tensor's storage."""
         L = _bind()
         children, node_iys = self.encoded()
         dtype = tensors[0].dtype
-        ptrs = (ctypes.c_void_p * len(tensors))(*[t.ptr for t in tensors])
-        nd = _i32([len(ix) for ix in self.ixs])
-        shapes = _i64([self.size_dict[l] for ix in self.ixs for l in ix])
-        strides = _i64([s for ix in self.ixs for s in _col([self.size_dict[l] for l in ix])])
-        ixs = _i32([l for ix in self.ixs for l in ix])
+        if views is None:
+            views = [(0, [self.size_dict[l] for l in ix], _col([self.size_dict[l] for l in ix]), ix)
+                     for ix in self.ixs]
+        es = np.dtype(dtype).itemsize
+        ptrs = (ctypes.c_void_p * len(tensors))(*[t.ptr + v[0] * es for t, v in zip(tensors, views)])
+        nd = _i32([len(v[3]) for v in views])
+        shapes = _i64([d for v in views for d in v[1]])
+        strides = _i64([d for v in views for d in v[2]])
+        ixs = _i32([l for v in views for l in v[3]])
         iy = _i32(self.iy)
         sl = _i32(list(self.size_dict.keys()))
         sv = _i64(list(self.size_dict.values()))
@@ -200,6 +205,24 @@ class Einsum:
         out = be.alloc(self.out_size(), tensors[0].dtype)
         self._call(be, alg, tensors, out, None)
         return out
+
+    def call_views(self, be: B200, alg, tensors, views, out, tape):
+        self._call(be, alg, tensors, out, tape, views)
+
+    def cost_and_gradient_views(self, be: B200, alg, tensors, views, dy):
+        """cost_and_gradient over strided views; gradients are contiguous in
+        each view's shape."""
+        out = be.alloc(self.out_size(), tensors[0].dtype)
+        tape = ctypes.c_void_p()
+        self._call(be, alg, tensors, out, ctypes.byref(tape), views)
+        try:
+            d = be.from_slice(np.asarray(dy, tensors[0].dtype))
+            grads = [be.alloc(max(1, int(np.prod(v[1]))), tensors[0].dtype) for v in views]
+            ptrs = (ctypes.c_void_p * len(grads))(*[g.ptr for g in grads])
+            _check(_bind().om_b200_einsum_backward(tape, d.ptr, ptrs))
+        finally:
+            _bind().om_b200_tape_free(tape)
+        return out, grads
 
     def cost_and_gradient(self, be: B200, alg, tensors, dy=None):
         """cost_and_gradient (backward.rs:769-799).  dy defaults to the
@@ -272,3 +295,97 @@ def ising_network(n: int, seed: int, beta: float = 1.0):
         tensors.append(np.asfortranarray(t).reshape(-1, order="F"))
     ixs = [[u, v] for u, v in edges]
     return ixs, [], {v: 2 for v in range(n)}, tensors, edges
+
+
+# ---------------------------------------------------------------------------
+# elimination-order trees (stand-in for omeco's TreeSA on graph networks)
+# ---------------------------------------------------------------------------
+def min_fill_order(ixs, iy, seed=0, restarts=16):
+    """Variable-elimination order by the min-fill heuristic with seeded random
+    tie-breaks; of `restarts` orders, the one with the smallest largest
+    elimination clique (then the smallest sum of 2^clique) is returned.
+    Labels of iy are never eliminated."""
+    rng = np.random.default_rng(seed)
+    labels = sorted({l for ix in ixs for l in ix} - set(iy))
+    base = {l: set() for l in labels}
+    for ix in ixs:
+        u = [l for l in set(ix) if l in base]
+        for a in u:
+            base[a].update(x for x in u if x != a)
+    best = None
+    for _ in range(restarts):
+        adj = {l: set(v) for l, v in base.items()}
+        order, width, total = [], 0, 0.0
+        alive = set(labels)
+        while alive:
+            cand, bestfill = [], None
+            for v in alive:
+                nb = list(adj[v])
+                fill = sum(1 for i in range(len(nb)) for j in range(i + 1, len(nb))
+                           if nb[j] not in adj[nb[i]])
+                if bestfill is None or fill < bestfill:
+                    cand, bestfill = [v], fill
+                elif fill == bestfill:
+                    cand.append(v)
+            cand.sort(key=lambda x: len(adj[x]))
+            m = len(adj[cand[0]])
+            cand = [c for c in cand if len(adj[c]) == m]
+            v = cand[int(rng.integers(len(cand)))]
+            nb = adj[v]
+            width = max(width, len(nb))
+            total += 2.0 ** len(nb)
+            for a in nb:
+                adj[a].update(x for x in nb if x != a)
+                adj[a].discard(v)
+            del adj[v]
+            alive.discard(v)
+            order.append(v)
+        key = (width, total)
+        if best is None or key < best[0]:
+            best = (key, order)
+    return best[1]
+
+
+def elimination_tree(ixs, iy, sizes, order):
+    """Binary contraction tree that follows an elimination order: eliminating
+    label v contracts every current tensor holding v, smallest first; the
+    remaining tensors are joined at the end."""
+    items = [(i, list(dict.fromkeys(ix))) for i, ix in enumerate(ixs)]
+    final = set(iy)
+
+    def size(ls):
+        s = 1
+        for l in ls:
+            s *= sizes[l]
+        return s
+
+    def join(a, b, rest):
+        outside = {l for _, ix in rest for l in ix} | final
+        out = [l for l in dict.fromkeys(a[1] + b[1]) if l in outside]
+        return ((a[0], b[0]), out)
+
+    for v in order:
+        hold = [it for it in items if v in it[1]]
+        if not hold:
+            continue
+        rest = [it for it in items if v not in it[1]]
+        while len(hold) > 1:
+            hold.sort(key=lambda it: size(it[1]))
+            a, b = hold[0], hold[1]
+            hold = hold[2:]
+            hold.append(join(a, b, rest + hold))
+        items = rest + hold
+    while len(items) > 1:
+        items.sort(key=lambda it: size(it[1]))
+        a, b = items[0], items[1]
+        items = items[2:] + [join(a, b, items[2:])]
+    return items[0][0]
+
+
+def best_tree(ixs, iy, sizes, seed=0, restarts=16):
+    """The better (smaller space, then time) of the greedy tree and the
+    min-fill elimination tree."""
+    t1 = greedy_tree(ixs, iy, sizes)
+    t2 = elimination_tree(ixs, iy, sizes, min_fill_order(ixs, iy, seed, restarts))
+    c1, c2 = tree_cost(t1, ixs, iy, sizes), tree_cost(t2, ixs, iy, sizes)
+    return t1 if (c1[1], c1[0]) <= (c2[1], c2[0]) else t2

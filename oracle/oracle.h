@@ -7,7 +7,7 @@
 extern "C" {
 #endif
 
-#define ORC_MAX_DIMS 32
+#define ORC_MAX_DIMS 64
 #define ORC_MAX_LABELS 4096
 
 enum { ORC_STANDARD = 0, ORC_MAXPLUS = 1, ORC_MINPLUS = 2, ORC_MAXMUL = 3 };

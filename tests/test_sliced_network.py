@@ -1,0 +1,97 @@
+"""Sliced network driver (omeinsum-rs_b200/network.py): slicing, per-rank
+slice assignment and the combine step, on CPU ranks (gloo, world size 2)
+with the oracle engine as the per-slice executor.  The GPU counterpart
+(DeviceExecutor on the B200) is in test_gpu_sliced_network.py."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from conftest import ROOT, load_pkg
+
+
+def _mods():
+    load_pkg()
+    import importlib
+    import engine as oe
+    return (importlib.import_module("omeinsum_b200.einsum"),
+            importlib.import_module("omeinsum_b200.network"), oe)
+
+
+def _case(kind):
+    E, N, oe = _mods()
+    if kind == "mis":
+        ixs, iy, sizes, ts, edges = E.mis_network(16, 9)
+        alg = "maxplus"
+    else:
+        ixs, iy, sizes, ts, edges = E.ising_network(14, 9)
+        alg = "standard"
+    tree = E.greedy_tree(ixs, iy, sizes)
+    sliced = N.choose_slices(ixs, iy, sizes, tree, 3, E.tree_cost)
+    return E, N, oe, alg, ixs, iy, sizes, ts, edges, tree, sliced
+
+
+def _worker(rank, world, port, kind, q):
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    E, N, oe, alg, ixs, iy, sizes, ts, edges, tree, sliced = _case(kind)
+    ex = N.OracleExecutor(oe, E, alg, ixs, iy, sizes, ts, tree)
+    v, g, win = N.run_sliced(ex, alg, ixs, sizes, sliced, rank, world, dist=dist)
+    q.put((rank, v, [x.tolist() for x in g], win))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("kind", ["mis", "ising"])
+def test_two_gloo_ranks_match_single_rank_and_unsliced(kind):
+    E, N, oe, alg, ixs, iy, sizes, ts, edges, tree, sliced = _case(kind)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, kind, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # single rank, same sliced schedule
+    ex = N.OracleExecutor(oe, E, alg, ixs, iy, sizes, ts, tree)
+    v1, g1, w1 = N.run_sliced(ex, alg, ixs, sizes, sliced, 0, 1)
+    ch, niy = E.encode_tree(tree, ixs, iy)
+    unsliced = oe.einsum(alg, ts, ixs, iy, sizes, ch, niy)[0]
+    for rank, v, g, win in res:
+        if kind == "mis":
+            assert v == v1 == unsliced and win == w1
+            for x, y in zip(g, g1):
+                np.testing.assert_array_equal(x, y)
+            sel = [int(np.asarray(x)[1] > np.asarray(x)[0]) for x in g[:16]]
+            assert sum(sel) == int(v) and all(not (sel[a] and sel[b]) for a, b in edges)
+        else:
+            assert abs(v - unsliced) <= 1e-12 * abs(unsliced)
+            for x, y in zip(g, g1):
+                np.testing.assert_allclose(x, y, rtol=1e-12, atol=1e-300)
+
+
+def test_order_key_is_monotone():
+    _, N, _ = _mods()
+    vals = [-np.inf, -3.5, -0.0, 0.0, 1e-30, 2.0, 7.0, np.inf]
+    keys = [N.order_key(v, False) for v in vals]
+    assert keys == sorted(keys)
+    keys = [N.order_key(v, True) for v in vals]
+    assert keys == sorted(keys, reverse=True)
