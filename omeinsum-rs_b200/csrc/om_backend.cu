@@ -125,6 +125,7 @@ int om_b200_create(int device, om_backend** out) {
     cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
   }
   e = cudaMalloc(&be->d_flags, 64);
+  if (e == cudaSuccess) e = cudaMemset(be->d_flags, 0, 64);
   if (e != cudaSuccess) {
     cudaStreamDestroy(be->stream);
     delete be;
@@ -174,6 +175,14 @@ int om_b200_stream(om_backend* be, void** stream_out) {
 int om_b200_sync(om_backend* be) {
   if (!be) return set_error(OM_ERR_INVALID, "om_b200_sync: null backend");
   OM_CUDA(cudaStreamSynchronize(be->stream), "cudaStreamSynchronize");
+  // error word of kernels with bounded waits (flags[1]): non-zero means a
+  // wait ran out and that kernel's output is not valid
+  uint32_t err = 0;
+  OM_CUDA(cudaMemcpy(&err, be->d_flags + 1, sizeof(err), cudaMemcpyDeviceToHost), "error word");
+  if (err) {
+    cudaMemset(be->d_flags + 1, 0, sizeof(err));
+    return set_error(OM_ERR_TIMEOUT, "a device wait ran out (tensor-core GEMM); results invalid");
+  }
   return OM_OK;
 }
 

@@ -21,6 +21,7 @@
 namespace om {
 
 int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled);
+int launch_gemm_tf32(om_backend* be, const GemmArgs& g, bool* handled);
 
 namespace {
 
@@ -180,6 +181,8 @@ int launch_gemm_exact(om_backend* be, const GemmArgs& g) {
 int launch_gemm(om_backend* be, const GemmArgs& g) {
   if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return OM_OK;
   bool handled = false;
+  OM_TRY(launch_gemm_tf32(be, g, &handled));
+  if (handled) return OM_OK;
   OM_TRY(launch_gemm_tropical_fast(be, g, &handled));
   if (handled) return OM_OK;
   return launch_gemm_exact(be, g);

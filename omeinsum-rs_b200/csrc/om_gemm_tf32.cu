@@ -1,0 +1,359 @@
+// K3: Standard f32 GEMM on the 5th-generation tensor cores (tcgen05, TMEM,
+// TMA) in a 3xTF32 split, for the reference's Standard<f32> contraction
+// (faer GEMM in src/backend/cpu/mod.rs:176-287,621-859).
+//
+// Every f32 operand x is split into hi = tf32(x) (round to nearest) and
+// lo = tf32(x - hi); the product is accumulated as
+//     A_lo B_hi + A_hi B_lo + A_hi B_hi
+// in f32 in tensor memory, which keeps the error near f32 rounding
+// (|error| ~ 2^-21 * sum_k |a||b|, inside the 1e-5 tolerance of the tests).
+//
+// Two kernels:
+//   split_tf32_kernel  one HBM pass: reads an operand through its strides
+//                      (any layout, batched), writes hi and lo as K-major
+//                      rows [batch][rows][Kp] (Kp = K rounded up to 32, zero
+//                      padded).  This is also the operand gather (K1) fused
+//                      with the split, staged through a 32 x 32 shared tile so
+//                      reads and writes stay coalesced.
+//   gemm_tf32x3_kernel one CTA per 128 x 128 output tile, 192 threads:
+//                      warp 0 issues TMA loads (cp.async.bulk.tensor, 128-byte
+//                      swizzle, no multicast) of the four 128 x 32 slabs
+//                      (A_hi, A_lo, B_hi, B_lo) into a 3-stage ring with
+//                      full / empty mbarriers; warp 1 allocates 128 TMEM
+//                      columns and one thread issues 12 tcgen05.mma kind::tf32
+//                      (M = N = 128, K = 8) per slab, committing each stage
+//                      back to the producer; warps 2..5 wait for the final
+//                      commit and move the f32 accumulator out with
+//                      tcgen05.ld.32x32b (warp w reads TMEM lanes 32*(w%4)..).
+// Every mbarrier wait is bounded; on expiry the kernel records an error word
+// that om_b200_sync reports, and every warp leaves after its own bounded
+// waits so that TMEM is always freed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "om_internal.h"
+
+namespace om {
+namespace {
+
+constexpr int TM = 128, TN = 128, TK = 32, STAGES = 3, NTH = 192;
+constexpr int SLAB_BYTES = TM * TK * 4;      // 16 KiB: 128 rows x 128 bytes
+constexpr int STAGE_BYTES = 4 * SLAB_BYTES;  // A_hi, A_lo, B_hi, B_lo
+constexpr uint32_t kWaitLimit = 1u << 24;    // polls of a try_wait before giving up
+
+// ---------------------------------------------------------------------------
+// split pre-pass
+// ---------------------------------------------------------------------------
+struct SplitArgs {
+  const float* x;
+  int64_t rows, K, Kp, batch;
+  int64_t sr, sk, sb;  // element strides of (row, k, batch)
+  float* hi;
+  float* lo;
+};
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+__global__ void split_tf32_kernel(SplitArgs a, int64_t tiles_k, int64_t tiles_r, int64_t total) {
+  __shared__ float tile[32][33];
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  const bool k_fast = a.sk == 1;
+  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    const int64_t tk = t % tiles_k, rest = t / tiles_k;
+    const int64_t tr = rest % tiles_r, b = rest / tiles_r;
+    const int64_t r0 = tr * 32, k0 = tk * 32;
+    const float* xb = a.x + b * a.sb;
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + (k_fast ? i : tx), k = k0 + (k_fast ? tx : i);
+      float v = 0.f;
+      if (r < a.rows && k < a.K) v = xb[r * a.sr + k * a.sk];
+      if (k_fast) tile[i][tx] = v;
+      else tile[tx][i] = v;
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + i, k = k0 + tx;
+      if (r < a.rows && k < a.Kp) {
+        const float v = tile[i][tx];
+        const float h = tf32_rna(v);
+        const int64_t o = (b * a.rows + r) * a.Kp + k;
+        a.hi[o] = h;
+        a.lo[o] = tf32_rna(v - h);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 GEMM
+// ---------------------------------------------------------------------------
+struct Tf32Args {
+  int M, N, T;
+  float* C;
+  int64_t scm, scn, scb;
+  uint32_t* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// K-major, 128-byte swizzle: 8-row groups 1024 B apart; k steps of 8 tf32
+// advance the start address by 32 B inside the swizzle atom
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+// kind::tf32, D f32, A/B tf32 K-major, M = 128, N = 128
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TN >> 3) << 17) |
+                            ((uint32_t)(TM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(NTH, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap ahi, const __grid_constant__ CUtensorMap alo,
+                       const __grid_constant__ CUtensorMap bhi, const __grid_constant__ CUtensorMap blo,
+                       Tf32Args g) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accum;
+  __shared__ uint32_t tmem_base;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN, bt = blockIdx.z;
+
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_base)),
+                 "r"(TN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[s])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&empty[s])));
+    }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&accum)));
+    asm volatile("fence.mbarrier_init.release.cluster;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = tmem_base;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      for (int t = 0; t < g.T && ok; ++t) {
+        const int s = t % STAGES;
+        if (t >= STAGES) ok = mbar_wait(smem_u32(&empty[s]), ((t / STAGES) - 1) & 1);
+        if (!ok) break;
+        const uint32_t bar = smem_u32(&full[s]);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                     "r"(STAGE_BYTES)
+                     : "memory");
+        const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
+        tma_load_3d(dst, &ahi, t * TK, m0, bt, bar);
+        tma_load_3d(dst + SLAB_BYTES, &alo, t * TK, m0, bt, bar);
+        tma_load_3d(dst + 2 * SLAB_BYTES, &bhi, t * TK, n0, bt, bar);
+        tma_load_3d(dst + 3 * SLAB_BYTES, &blo, t * TK, n0, bt, bar);
+      }
+      if (!ok) atomicOr(g.err, 1u);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      for (int t = 0; t < g.T && ok; ++t) {
+        const int s = t % STAGES;
+        ok = mbar_wait(smem_u32(&full[s]), (t / STAGES) & 1);
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+#pragma unroll
+        for (int j = 0; j < TK / 8; ++j) {
+          const uint64_t a_h = sw128_desc(base + j * 32);
+          const uint64_t a_l = sw128_desc(base + SLAB_BYTES + j * 32);
+          const uint64_t b_h = sw128_desc(base + 2 * SLAB_BYTES + j * 32);
+          const uint64_t b_l = sw128_desc(base + 3 * SLAB_BYTES + j * 32);
+          mma_tf32(tmem, a_l, b_h, (t > 0 || j > 0) ? 1u : 0u);
+          mma_tf32(tmem, a_h, b_l, 1u);
+          mma_tf32(tmem, a_h, b_h, 1u);
+        }
+        mma_commit(smem_u32(&empty[s]));
+      }
+      mma_commit(smem_u32(&accum));  // fires once every issued MMA has completed
+      if (!ok) atomicOr(g.err, 1u);
+    }
+  } else {  // epilogue warps 2..5
+    ok = mbar_wait(smem_u32(&accum), 0);
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    if (ok) {
+      const int quad = warp & 3;
+      const int m = m0 + 32 * quad + lane;
+      float* Cb = g.C + (int64_t)bt * g.scb;
+#pragma unroll 1
+      for (int c0 = 0; c0 < TN; c0 += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+            "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+              "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+              "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
+              "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+              "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+              "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (m < g.M) {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            const int n = n0 + c0 + q;
+            if (n < g.N) Cb[(int64_t)m * g.scm + (int64_t)n * g.scn] = __uint_as_float(r[q]);
+          }
+        }
+      }
+    } else if (lane == 0) {
+      atomicOr(g.err, 1u);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TN));
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+// 3-D map over a split operand [batch][rows][Kp] f32, box 32 (k) x 128 rows
+int make_map(CUtensorMap* map, float* base, int64_t rows, int64_t Kp, int64_t batch) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(OM_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+  cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(Kp * 4), (cuuint64_t)(rows * Kp * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)TK, (cuuint32_t)TM, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(OM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return OM_OK;
+}
+
+int launch_split(om_backend* be, const float* x, int64_t rows, int64_t K, int64_t Kp,
+                 int64_t batch, int64_t sr, int64_t sk, int64_t sb, float* hi, float* lo) {
+  SplitArgs a{x, rows, K, Kp, batch, sr, sk, sb, hi, lo};
+  const int64_t tk = Kp / 32, tr = (rows + 31) / 32, total = tk * tr * batch;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(total, (int64_t)be->num_sms * 16));
+  ProfScope prof(be, "split_tf32");
+  split_tf32_kernel<<<blocks, dim3(32, 8), 0, be->stream>>>(a, tk, tr, total);
+  note_launch();
+  return check_cuda(cudaGetLastError(), "split_tf32 launch");
+}
+
+}  // namespace
+
+// Takes a Standard f32 GEMM when the tensor-core path applies.
+int launch_gemm_tf32(om_backend* be, const GemmArgs& g, bool* handled) {
+  *handled = false;
+  if (g.dtype != OM_F32 || g.alg != OM_STANDARD || g.argmax) return OM_OK;
+  if (g.M < 64 || g.N < 64 || g.K < 16 || g.batch > 65535) return OM_OK;
+  if (g.M > (1 << 30) || g.N > (1 << 30) || g.K > (1 << 30)) return OM_OK;
+  static const bool disabled = getenv("OM_DISABLE_TCGEN05") != nullptr;
+  if (disabled) return OM_OK;
+  const int64_t Kp = (g.K + TK - 1) / TK * TK;
+  const size_t na = (size_t)(g.batch * g.M * Kp), nb = (size_t)(g.batch * g.N * Kp);
+  Scratch ws;
+  OM_TRY(ws.alloc(be, 4 * (2 * na + 2 * nb)));
+  float* a_hi = (float*)ws.ptr;
+  float* a_lo = a_hi + na;
+  float* b_hi = a_lo + na;
+  float* b_lo = b_hi + nb;
+  OM_TRY(launch_split(be, (const float*)g.A, g.M, g.K, Kp, g.batch, g.sam, g.sak, g.sab, a_hi, a_lo));
+  OM_TRY(launch_split(be, (const float*)g.B, g.N, g.K, Kp, g.batch, g.sbn, g.sbk, g.sbb, b_hi, b_lo));
+  CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+  OM_TRY(make_map(&m_ahi, a_hi, g.M, Kp, g.batch));
+  OM_TRY(make_map(&m_alo, a_lo, g.M, Kp, g.batch));
+  OM_TRY(make_map(&m_bhi, b_hi, g.N, Kp, g.batch));
+  OM_TRY(make_map(&m_blo, b_lo, g.N, Kp, g.batch));
+  Tf32Args a;
+  a.M = (int)g.M;
+  a.N = (int)g.N;
+  a.T = (int)(Kp / TK);
+  a.C = (float*)g.C;
+  a.scm = g.scm;
+  a.scn = g.scn;
+  a.scb = g.scb;
+  a.err = be->d_flags + 1;
+  const size_t smem = (size_t)STAGES * STAGE_BYTES + 1024;
+  OM_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem),
+          "cudaFuncSetAttribute(tf32)");
+  dim3 grid((a.M + TM - 1) / TM, (a.N + TN - 1) / TN, (unsigned)g.batch);
+  {
+    ProfScope prof(be, "gemm_tf32x3_tcgen05");
+    gemm_tf32x3_kernel<<<grid, NTH, smem, be->stream>>>(m_ahi, m_alo, m_bhi, m_blo, a);
+    note_launch();
+    OM_CUDA(cudaGetLastError(), "gemm_tf32x3 launch");
+  }
+  *handled = true;
+  return OM_OK;
+}
+
+}  // namespace om
