@@ -163,6 +163,44 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_permuted(be, om, local_rank):
+    """'abcd,dcef->abfe', a=b=e=f=64, c=d=32, f32 N(0,1),
+    as Standard (tensor cores, 3xTF32) and as MinPlus; device-timed per
+    om_b200_contract call (kernels per class from the profiler)."""
+    import oracle as orc
+    import torch
+    a_, c_ = 64, 32
+    sa, sb = [a_, a_, c_, c_], [c_, c_, a_, a_]
+    A = be.from_slice(orc.normal(SEED + 2, a_ * a_ * c_ * c_))
+    B = be.from_slice(orc.normal(SEED + 3, c_ * c_ * a_ * a_))
+    C = be.alloc(a_ ** 4, np.float32)
+    col = om.col_strides
+    flops = 2.0 * 4096 * 4096 * 1024
+    out = {"workload": "abcd,dcef->abfe a=b=e=f=64 c=d=32 f32", "unit": "TFLOP/s (TOP/s)"}
+    stream = torch.cuda.ExternalStream(be.stream(), device=local_rank)
+    for alg in ("standard", "minplus"):
+        def call():
+            be.contract_into(alg, A, sa, col(sa), [0, 1, 2, 3], B, sb, col(sb), [3, 2, 4, 5],
+                             [a_] * 4, [0, 1, 5, 4], C, None)
+        for _ in range(3):
+            call()
+        be.synchronize()
+        be.profile(True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record(stream)
+        for _ in range(reps):
+            call()
+        e1.record(stream)
+        be.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        prof = be.profile_report()
+        be.profile(False)
+        out[alg] = {"ms_per_call": round(ms, 4), "value": round(flops / (ms / 1e3) / 1e12, 2),
+                    "kernels_ms": {k: round(v[0] / v[1], 4) for k, v in prof.items()}}
+    return out
+
+
 NET_N, NET_SLICED = 190, 3
 
 
@@ -309,6 +347,7 @@ def run_b200(args, rank, world, local_rank):
         torch.distributed.all_reduce(t_e2e, op=torch.distributed.ReduceOp.MAX)
     e2e_value = world * args.steps * OPS / float(t_e2e.item()) / 1e9
 
+    permuted = run_permuted(be, om, local_rank) if rank == 0 else None
     network = run_network(be, om, world, rank, local_rank, args)
     if rank != 0:
         return
@@ -348,6 +387,7 @@ def run_b200(args, rank, world, local_rank):
                                    f"full k), reference loop order, {cpu_dt:.1f} s"},
         "clocks": clk.summary(),
         "network": network,
+        "permuted": permuted,
     }
     print(json.dumps(line), flush=True)
     be.close()
