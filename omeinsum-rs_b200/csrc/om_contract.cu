@@ -230,6 +230,53 @@ int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Op
   rfree = choose_order(rfree, {&B, &C}, false);
   batch = choose_order(batch, {&A, &B, &C}, false);
 
+  // Small, batched shapes (tensor-network nodes) whose operands or output do
+  // not flatten are contracted in place by decoding every mode, instead of
+  // gathering: for these memory-bound nodes the gathers would cost more than
+  // the contraction itself.
+  {
+    const int64_t M0 = group_size(A, lfree), N0 = group_size(B, rfree);
+    // thread per output: the shapes the small GEMM kernel takes anyway
+    const bool small = (M0 * N0 <= 1024) || M0 < 16 || N0 < 16;
+    const bool flat = flat_stride(A, lfree) >= 0 && flat_stride(A, contr) >= 0 &&
+                      flat_stride(A, batch) >= 0 && flat_stride(B, contr) >= 0 &&
+                      flat_stride(B, rfree) >= 0 && flat_stride(B, batch) >= 0 &&
+                      flat_stride(C, lfree) >= 0 && flat_stride(C, rfree) >= 0 &&
+                      flat_stride(C, batch) >= 0;
+    const bool fits = lfree.size() <= (size_t)kMaxGroupModes && rfree.size() <= (size_t)kMaxGroupModes &&
+                      contr.size() <= (size_t)kMaxGroupModes && batch.size() <= (size_t)kMaxGroupModes;
+    if (small && !flat && fits) {
+      StridedGemmArgs sg{};
+      sg.alg = alg;
+      sg.dtype = dt;
+      sg.M = M0;
+      sg.N = N0;
+      sg.K = group_size(A, contr);
+      sg.batch = group_size(A, batch);
+      sg.A = a;
+      sg.B = b;
+      sg.C = c_out;
+      sg.argmax = argmax;
+      auto fill = [&](ModeGroup& grp, const std::vector<int32_t>& modes, const Operand* o0,
+                      const Operand* o1, const Operand* o2) {
+        grp.n = (int)modes.size();
+        for (size_t j = 0; j < modes.size(); ++j) {
+          const int32_t md = modes[j];
+          const Operand* ref = o0->pos(md) >= 0 ? o0 : o1;
+          grp.ext[j] = ref->shape[ref->pos(md)];
+          grp.s0[j] = o0 ? o0->strides[o0->pos(md)] : 0;
+          grp.s1[j] = o1 ? o1->strides[o1->pos(md)] : 0;
+          grp.s2[j] = o2 ? o2->strides[o2->pos(md)] : 0;
+        }
+      };
+      fill(sg.gm, lfree, &A, &C, nullptr);
+      fill(sg.gn, rfree, &B, &C, nullptr);
+      fill(sg.gk, contr, &A, &B, nullptr);
+      fill(sg.gb, batch, &A, &B, &C);
+      return launch_gemm_small_strided(be, sg);
+    }
+  }
+
   Scratch ga, gb;
   if (flat_stride(A, lfree) < 0 || flat_stride(A, contr) < 0 || flat_stride(A, batch) < 0) {
     Operand g;

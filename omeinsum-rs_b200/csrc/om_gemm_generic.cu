@@ -142,6 +142,97 @@ __global__ void __launch_bounds__(256) gemm_small(GemmArgs g, int64_t total) {
   }
 }
 
+// One thread per output element; every group index is decoded into the
+// operands' offsets mode by mode, so operands whose groups do not flatten are
+// read in place (no gather).  The contracted offsets of A and B are tabulated
+// per block in shared memory when K is small.
+constexpr int kKTable = 1024;
+
+__device__ __forceinline__ void decode2(const ModeGroup& g, int64_t i, int64_t& o0, int64_t& o1) {
+  for (int j = 0; j < g.n; ++j) {
+    const int64_t d = i % g.ext[j];
+    i /= g.ext[j];
+    o0 += d * g.s0[j];
+    o1 += d * g.s1[j];
+  }
+}
+
+template <typename T, int ALG, bool ARGMAX>
+__global__ void __launch_bounds__(256) gemm_small_strided(StridedGemmArgs g, int64_t total) {
+  using S = Semi<ALG, T>;
+  __shared__ int64_t ka[kKTable], kb[kKTable];
+  const bool table = g.K <= kKTable;
+  if (table) {
+    for (int64_t k = threadIdx.x; k < g.K; k += blockDim.x) {
+      int64_t oa = 0, ob = 0;
+      decode2(g.gk, k, oa, ob);
+      ka[k] = oa;
+      kb[k] = ob;
+    }
+    __syncthreads();
+  }
+  const T* __restrict__ A = (const T*)g.A;
+  const T* __restrict__ B = (const T*)g.B;
+  T* __restrict__ C = (T*)g.C;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = e % g.M, r = e / g.M, n = r % g.N, bt = r / g.N;
+    int64_t oa = 0, ob = 0, oc = 0, t0 = 0;
+    decode2(g.gm, m, oa, oc);
+    decode2(g.gn, n, ob, oc);
+    {
+      int64_t i = bt;
+      for (int j = 0; j < g.gb.n; ++j) {
+        const int64_t d = i % g.gb.ext[j];
+        i /= g.gb.ext[j];
+        oa += d * g.gb.s0[j];
+        ob += d * g.gb.s1[j];
+        oc += d * g.gb.s2[j];
+      }
+    }
+    T acc = S::zero();
+    uint32_t idx = 0;
+    for (int64_t k = 0; k < g.K; ++k) {
+      int64_t xa, xb;
+      if (table) {
+        xa = ka[k];
+        xb = kb[k];
+      } else {
+        xa = 0;
+        xb = 0;
+        decode2(g.gk, k, xa, xb);
+      }
+      const T av = A[oa + xa], bv = B[ob + xb];
+      if (ALG == OM_STANDARD) {
+        acc = fma(av, bv, acc);
+      } else {
+        const T p = S::mul(av, bv);
+        if (!S::keep(acc, p)) {
+          acc = p;
+          idx = (uint32_t)k;
+        }
+      }
+    }
+    (void)t0;
+    C[oc] = acc;
+    if (ARGMAX) g.argmax[oc] = (ALG == OM_STANDARD) ? 0u : idx;
+  }
+}
+
+template <typename T, int ALG>
+int launch_strided_typed(om_backend* be, const StridedGemmArgs& g) {
+  const int64_t total = g.M * g.N * g.batch;
+  int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)be->num_sms * 64);
+  if (blocks < 1) blocks = 1;
+  ProfScope prof(be, "gemm_small_strided");
+  if (g.argmax)
+    gemm_small_strided<T, ALG, true><<<(int)blocks, 256, 0, be->stream>>>(g, total);
+  else
+    gemm_small_strided<T, ALG, false><<<(int)blocks, 256, 0, be->stream>>>(g, total);
+  note_launch();
+  return check_cuda(cudaGetLastError(), "gemm_small_strided launch");
+}
+
 template <typename T, int ALG>
 int launch_typed(om_backend* be, const GemmArgs& g) {
   const int64_t outputs = g.M * g.N * g.batch;
@@ -174,6 +265,16 @@ int launch_gemm_exact(om_backend* be, const GemmArgs& g) {
     OM_DISPATCH_ALG(g.alg, ALG, return launch_typed<float, ALG>(be, g));
   } else if (g.dtype == OM_F64) {
     OM_DISPATCH_ALG(g.alg, ALG, return launch_typed<double, ALG>(be, g));
+  }
+  return set_error(OM_ERR_UNSUPPORTED, "gemm: dtype must be f32 or f64");
+}
+
+int launch_gemm_small_strided(om_backend* be, const StridedGemmArgs& g) {
+  if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return OM_OK;
+  if (g.dtype == OM_F32) {
+    OM_DISPATCH_ALG(g.alg, ALG, return launch_strided_typed<float, ALG>(be, g));
+  } else if (g.dtype == OM_F64) {
+    OM_DISPATCH_ALG(g.alg, ALG, return launch_strided_typed<double, ALG>(be, g));
   }
   return set_error(OM_ERR_UNSUPPORTED, "gemm: dtype must be f32 or f64");
 }

@@ -93,6 +93,29 @@ struct GemmArgs {
 };
 int launch_gemm(om_backend* be, const GemmArgs& g);
 
+// A mode group decoded element by element: index i of the group is the
+// column-major number over its modes (extents ext), and contributes
+// sum_j digit_j * s<op>[j] to each operand's offset.
+constexpr int kMaxGroupModes = 16;
+struct ModeGroup {
+  int n = 0;
+  int64_t ext[kMaxGroupModes];
+  int64_t s0[kMaxGroupModes], s1[kMaxGroupModes], s2[kMaxGroupModes];
+};
+// Batched small GEMM over strided operands whose groups need not flatten:
+// gm strides (A, C), gn (B, C), gk (A, B), gb (A, B, C).
+struct StridedGemmArgs {
+  om_algebra alg;
+  om_dtype dtype;
+  int64_t M, N, K, batch;
+  const void* A;
+  const void* B;
+  void* C;
+  uint32_t* argmax;
+  ModeGroup gm, gn, gk, gb;
+};
+int launch_gemm_small_strided(om_backend* be, const StridedGemmArgs& g);
+
 // Unary einsum (trace / diagonal / reduce / permute / embed).
 int launch_unary(om_backend* be, om_algebra alg, om_dtype dt, const void* x, int nx,
                  const int32_t* ix, const int64_t* shape_x, const int64_t* strides_x, int ny,
