@@ -98,6 +98,10 @@ struct FastArgs {
   uint32_t* argmax;
   const uint32_t* gate;
   uint32_t* ws;  // argmax: per-CTA, per-slab, per-thread improvement bitmasks
+  int tiles, gx, gy, max_units;  // stream-K work split
+  float* part_v;                 // [2 per CTA][NE][NT] piece values
+  uint32_t* part_k;              // [2 per CTA][NE][NT] piece first winning k
+  uint32_t* arrivals;            // [tiles] pieces of a cut tile finished so far
 };
 
 // float index of element (row, k) in a k-pair slab of width W
@@ -255,6 +259,68 @@ __device__ __forceinline__ int col_of(int warp, int lane, int j) {
   return 16 * (warp >> 1) + 2 * (lane >> 3) + (j & 1) + 8 * (j >> 1);
 }
 
+constexpr uint32_t kNoK = 0xffffffffu;  // partial piece that never beat zero()
+
+// Persistent, stream-K work split: the (tile, slab) units of the whole GEMM
+// are cut into gridDim.x equal contiguous ranges, one per CTA, so every CTA
+// does the same amount of work whatever the tile count (no partly empty last
+// wave).  A tile cut between CTAs is computed as pieces (slab ranges); each
+// piece writes its value and first winning k to a partial slot, and the CTA
+// whose piece arrives last (a per-tile atomic counter; nobody waits) merges
+// the pieces in k order.
+__device__ __forceinline__ int64_t unit_begin(int64_t c, int64_t W, int64_t G) { return c * W / G; }
+
+// Merges the pieces of a tile that was cut between CTAs, in k order: a later
+// piece replaces the running result only when strictly better, so the first k
+// reaching the maximum wins, as in generic_gemm_with_argmax.  Run by the CTA
+// that finishes the tile's last piece.
+template <int ALG, bool ARGMAX>
+__device__ __forceinline__ void merge_tile(const FastArgs& g, int tile, int64_t G, int warp,
+                                           int lane, int tid) {
+  const int64_t W = (int64_t)g.tiles * g.T;
+  const int64_t ua = (int64_t)tile * g.T, ub = ua + g.T - 1;
+  const int64_t c_first = ((ua + 1) * G + W - 1) / W - 1;  // owner of unit ua
+  const int64_t c_last = ((ub + 1) * G + W - 1) / W - 1;
+  const int bx = tile % g.gx, by = (tile / g.gx) % g.gy, bt = tile / (g.gx * g.gy);
+  const int m0 = bx * TB_M, n0 = by * TB_N;
+  const int64_t cbase = (int64_t)bt * g.scb;
+  const float z = Semi<ALG, float>::zero();
+  float best[NE];
+  uint32_t kbest[NE];
+#pragma unroll
+  for (int e = 0; e < NE; ++e) {
+    best[e] = z;
+    kbest[e] = kNoK;
+  }
+  for (int64_t cc = c_first; cc <= c_last; ++cc) {
+    const size_t base = (size_t)(cc * 2 + (unit_begin(cc, W, G) < ua ? 1 : 0)) * NE * NT + tid;
+#pragma unroll
+    for (int e = 0; e < NE; ++e) {
+      const float v = __ldcg(g.part_v + base + (size_t)e * NT);
+      if (ARGMAX) {
+        const uint32_t k = __ldcg(g.part_k + base + (size_t)e * NT);
+        if (k != kNoK && improved<ALG>(v, best[e])) {
+          best[e] = v;
+          kbest[e] = k;
+        }
+      } else {
+        best[e] = (ALG == OM_MINPLUS) ? fminf(best[e], v) : fmaxf(best[e], v);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < NE; ++e) {
+    const int m = m0 + row_of(warp, lane, e >> 2), n = n0 + col_of(warp, lane, e & 3);
+    if (m < g.M && n < g.N) {
+      const int64_t off = cbase + (int64_t)m * g.scm + (int64_t)n * g.scn;
+      float v = best[e];
+      if (ALG == OM_MAXMUL && v == 0.f) v = 0.f;
+      g.C[off] = v;
+      if (ARGMAX) g.argmax[off] = kbest[e] == kNoK ? 0u : kbest[e];
+    }
+  }
+}
+
 template <int ALG, bool ARGMAX, bool A_MC, bool B_KC>
 __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
   if (fast_path_ruled_out(*g.gate, ALG)) return;
@@ -262,165 +328,205 @@ __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
   float* As0 = (float*)smem;           // 2 x TB_K*TB_M floats
   float* Bs0 = As0 + 2 * TB_K * TB_M;  // 2 x TB_K*TB_N floats
   float* vals = (float*)smem + resolve_region<A_MC, B_KC>();  // [NE][NT] (ARGMAX)
+  uint32_t* kres = (uint32_t*)vals;  // resolved k of an output overwrites its value
   uint32_t* stage = (uint32_t*)(vals + NE * NT);              // [8 warps][64] items
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int m0 = blockIdx.x * TB_M, n0 = blockIdx.y * TB_N;
-  const int bt = blockIdx.z;
-  const float* Ab = g.A + bt * g.sab;
-  const float* Bb = g.B + bt * g.sbb;
-  uint32_t* masks = g.ws + ((size_t)(bt * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) *
-                               (size_t)g.T * NT;
   const int r0 = row_of(warp, lane, 0), c0 = col_of(warp, lane, 0);
-
-  float acc[8][4];
+  const int64_t G = gridDim.x, c = blockIdx.x;
+  const int64_t W = (int64_t)g.tiles * g.T;
+  const int64_t u0 = unit_begin(c, W, G), u1 = unit_begin(c + 1, W, G);
+  uint32_t* masks = g.ws + (size_t)c * g.max_units * NT;
   const float z = Semi<ALG, float>::zero();
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = z;
+  __shared__ bool last_piece;
 
-  Stager<ALG, A_MC, B_KC> st;
-  st.load(g, Ab, Bb, m0, n0, 0, tid);
-  st.store(As0, Bs0, tid);
-  __syncthreads();
+  for (int64_t u = u0; u < u1;) {
+    const int tile = (int)(u / g.T);
+    const int tb = (int)(u % g.T);
+    const int64_t rem_units = u1 - u;
+    const int te = (int)(tb + rem_units < g.T ? tb + rem_units : g.T);
+    u += te - tb;
+    const int bx = tile % g.gx, by = (tile / g.gx) % g.gy, bt = tile / (g.gx * g.gy);
+    const int m0 = bx * TB_M, n0 = by * TB_N;
+    const float* Ab = g.A + bt * g.sab;
+    const float* Bb = g.B + bt * g.sbb;
 
-  for (int t = 0; t < g.T; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < g.T) st.load(g, Ab, Bb, m0, n0, (t + 1) * TB_K, tid);
-    const float* As = As0 + buf * TB_K * TB_M;
-    const float* Bs = Bs0 + buf * TB_K * TB_N;
-    float before[8][4];
-    if (ARGMAX) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) before[i][j] = acc[i][j];
-    }
-#pragma unroll 4
-    for (int kp = 0; kp < TB_K / 2; ++kp) {
-      const float* arow = As + kp * TB_M * 2 + 2 * r0;
-      const float* brow = Bs + kp * TB_N * 2 + 2 * c0;
-      unsigned long long a[8], b[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const ulonglong2 v = *(const ulonglong2*)(arow + 32 * q);
-        a[2 * q] = v.x;
-        a[2 * q + 1] = v.y;
-      }
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const ulonglong2 v = *(const ulonglong2*)(brow + 16 * q);
-        b[2 * q] = v.x;
-        b[2 * q + 1] = v.y;
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float lo, hi;
-          unpack(tmul2<ALG>(a[i], b[j]), lo, hi);
-          acc[i][j] = tfold3<ALG>(acc[i][j], lo, hi);
-        }
-    }
-    if (ARGMAX) {
-      uint32_t bits = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (improved<ALG>(acc[i][j], before[i][j])) bits |= 1u << (i * 4 + j);
-      masks[(size_t)t * NT + tid] = bits;
-    }
-    if (t + 1 < g.T) st.store(As0 + (buf ^ 1) * TB_K * TB_M, Bs0 + (buf ^ 1) * TB_K * TB_N, tid);
-    __syncthreads();
-  }
-
-  const int64_t cbase = (int64_t)bt * g.scb;
-  uint32_t remaining = 0xffffffffu;  // outputs whose deciding slab is not found yet
-  if (ARGMAX) {
+    float acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) vals[(i * 4 + j) * NT + tid] = acc[i][j];
-    uint32_t* items = stage + warp * 64;
-    // Resolve pass, last slab first: the deciding slab of an output is the
-    // last one whose bit is set.  Items of a slab are compacted across the
-    // warp so every lane scans at most one output per round.
-    using RS = ResolveStager<A_MC, B_KC>;
-    RS rs;
-    auto stA = [&](int q) { return (float*)smem + q * RS::STAGE; };
-    auto stB = [&](int q) { return (float*)smem + q * RS::STAGE + RS::A_FLOATS; };
-    rs.issue(g, Ab, Bb, m0, n0, g.T - 1, stA(0), stB(0), tid);
-    uint32_t mask_next = masks[(size_t)(g.T - 1) * NT + tid];
-    for (int t = g.T - 1; t >= 0; --t) {
-      const int s = (g.T - 1 - t) & 1;
-      const float* RA = stA(s);
-      const float* RB = stB(s);
-      const uint32_t mine = mask_next & remaining;
-      if (t >= 1) {
-        rs.issue(g, Ab, Bb, m0, n0, t - 1, stA(s ^ 1), stB(s ^ 1), tid);
-        mask_next = masks[(size_t)(t - 1) * NT + tid];
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
-      }
-      __syncthreads();
-      remaining &= ~mine;
-      const int cnt = __popc(mine);
-      int pos = cnt;  // inclusive warp scan
+      for (int j = 0; j < 4; ++j) acc[i][j] = z;
+
+    Stager<ALG, A_MC, B_KC> st;
+    __syncthreads();  // the previous piece may still read shared memory
+    st.load(g, Ab, Bb, m0, n0, tb * TB_K, tid);
+    st.store(As0, Bs0, tid);
+    __syncthreads();
+
+    for (int t = tb; t < te; ++t) {
+      const int buf = (t - tb) & 1;
+      if (t + 1 < te) st.load(g, Ab, Bb, m0, n0, (t + 1) * TB_K, tid);
+      const float* As = As0 + buf * TB_K * TB_M;
+      const float* Bs = Bs0 + buf * TB_K * TB_N;
+      float before[8][4];
+      if (ARGMAX) {
 #pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, pos, d);
-        if (lane >= d) pos += v;
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) before[i][j] = acc[i][j];
       }
-      const int total = __shfl_sync(0xffffffffu, pos, 31);
-      const int kmax = min(TB_K, g.K - t * TB_K);
-      for (int done = 0; done < total; done += 64) {
-        uint32_t rest = mine;
-        int p = pos - cnt;
-        while (rest) {
-          const int e = __ffs(rest) - 1;
-          rest &= rest - 1;
-          if (p >= done && p < done + 64) items[p - done] = ((uint32_t)lane << 5) | (uint32_t)e;
-          ++p;
+#pragma unroll 4
+      for (int kp = 0; kp < TB_K / 2; ++kp) {
+        const float* arow = As + kp * TB_M * 2 + 2 * r0;
+        const float* brow = Bs + kp * TB_N * 2 + 2 * c0;
+        unsigned long long a[8], b[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const ulonglong2 v = *(const ulonglong2*)(arow + 32 * q);
+          a[2 * q] = v.x;
+          a[2 * q + 1] = v.y;
         }
-        __syncwarp();
-        const int here = min(64, total - done);
-        for (int q = lane; q < here; q += 32) {
-          const uint32_t it = items[q];
-          const int src = (int)(it >> 5), e = (int)(it & 31);
-          const int mi = row_of(warp, src, e >> 2), nj = col_of(warp, src, e & 3);
-          const float v = vals[e * NT + warp * 32 + src];
-          int kb = 0;
 #pragma unroll
-          for (int kk = TB_K - 1; kk >= 0; --kk) {
-            const float pr = tmul<ALG>(RA[RS::a_at(mi, kk)], RB[RS::b_at(nj, kk)]);
-            if (kk < kmax && pr == v) kb = kk;
+        for (int q = 0; q < 2; ++q) {
+          const ulonglong2 v = *(const ulonglong2*)(brow + 16 * q);
+          b[2 * q] = v.x;
+          b[2 * q + 1] = v.y;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float lo, hi;
+            unpack(tmul2<ALG>(a[i], b[j]), lo, hi);
+            acc[i][j] = tfold3<ALG>(acc[i][j], lo, hi);
           }
-          const int m = m0 + mi, n = n0 + nj;
-          if (m < g.M && n < g.N)
-            g.argmax[cbase + (int64_t)m * g.scm + (int64_t)n * g.scn] = (uint32_t)(t * TB_K + kb);
+      }
+      if (ARGMAX) {
+        uint32_t bits = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (improved<ALG>(acc[i][j], before[i][j])) bits |= 1u << (i * 4 + j);
+        masks[(size_t)(t - tb) * NT + tid] = bits;
+      }
+      if (t + 1 < te)
+        st.store(As0 + (buf ^ 1) * TB_K * TB_M, Bs0 + (buf ^ 1) * TB_K * TB_N, tid);
+      __syncthreads();
+    }
+
+    uint32_t remaining = 0xffffffffu;  // outputs whose deciding slab is not found yet
+    if (ARGMAX) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) vals[(i * 4 + j) * NT + tid] = acc[i][j];
+      uint32_t* items = stage + warp * 64;
+      // Resolve pass over the piece's slabs, last first: the deciding slab of
+      // an output is the last one whose bit is set.  Items of a slab are
+      // compacted across the warp so every lane scans at most one output per
+      // round; the found k replaces the output's value in shared memory.
+      using RS = ResolveStager<A_MC, B_KC>;
+      RS rs;
+      auto stA = [&](int q) { return (float*)smem + q * RS::STAGE; };
+      auto stB = [&](int q) { return (float*)smem + q * RS::STAGE + RS::A_FLOATS; };
+      rs.issue(g, Ab, Bb, m0, n0, te - 1, stA(0), stB(0), tid);
+      uint32_t mask_next = masks[(size_t)(te - 1 - tb) * NT + tid];
+      for (int t = te - 1; t >= tb; --t) {
+        const int s = (te - 1 - t) & 1;
+        const float* RA = stA(s);
+        const float* RB = stB(s);
+        const uint32_t mine = mask_next & remaining;
+        if (t > tb) {
+          rs.issue(g, Ab, Bb, m0, n0, t - 1, stA(s ^ 1), stB(s ^ 1), tid);
+          mask_next = masks[(size_t)(t - 1 - tb) * NT + tid];
+          cp_async_wait<1>();
+        } else {
+          cp_async_wait<0>();
         }
-        __syncwarp();
+        __syncthreads();
+        remaining &= ~mine;
+        const int cnt = __popc(mine);
+        int pos = cnt;  // inclusive warp scan
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, pos, d);
+          if (lane >= d) pos += v;
+        }
+        const int total = __shfl_sync(0xffffffffu, pos, 31);
+        const int kmax = min(TB_K, g.K - t * TB_K);
+        for (int done = 0; done < total; done += 64) {
+          uint32_t rest = mine;
+          int p = pos - cnt;
+          while (rest) {
+            const int e = __ffs(rest) - 1;
+            rest &= rest - 1;
+            if (p >= done && p < done + 64) items[p - done] = ((uint32_t)lane << 5) | (uint32_t)e;
+            ++p;
+          }
+          __syncwarp();
+          const int here = min(64, total - done);
+          for (int q = lane; q < here; q += 32) {
+            const uint32_t it = items[q];
+            const int src = (int)(it >> 5), e = (int)(it & 31);
+            const int mi = row_of(warp, src, e >> 2), nj = col_of(warp, src, e & 3);
+            const int slot = e * NT + warp * 32 + src;
+            const float v = vals[slot];
+            int kb = 0;
+#pragma unroll
+            for (int kk = TB_K - 1; kk >= 0; --kk) {
+              const float pr = tmul<ALG>(RA[RS::a_at(mi, kk)], RB[RS::b_at(nj, kk)]);
+              if (kk < kmax && pr == v) kb = kk;
+            }
+            kres[slot] = (uint32_t)(t * TB_K + kb);
+          }
+          __syncwarp();
+        }
+        __syncthreads();
+      }
+    }
+
+    const bool whole = tb == 0 && te == g.T;
+    const int64_t cbase = (int64_t)bt * g.scb;
+    const int pslot = (int)(c * 2 + (tb == (int)(u0 % g.T) && tile == (int)(u0 / g.T) ? 0 : 1));
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int e = i * 4 + j;
+        float v = acc[i][j];
+        uint32_t k = kNoK;
+        if (ARGMAX && !((remaining >> e) & 1u)) k = kres[e * NT + tid];
+        if (whole) {
+          const int m = m0 + row_of(warp, lane, i), n = n0 + col_of(warp, lane, j);
+          if (m < g.M && n < g.N) {
+            const int64_t off = cbase + (int64_t)m * g.scm + (int64_t)n * g.scn;
+            if (ALG == OM_MAXMUL && v == 0.f) v = 0.f;  // zero() is +0; a -0 product never wins
+            g.C[off] = v;
+            if (ARGMAX) g.argmax[off] = k == kNoK ? 0u : k;
+          }
+        } else {
+          g.part_v[((size_t)pslot * NE + e) * NT + tid] = v;
+          if (ARGMAX) g.part_k[((size_t)pslot * NE + e) * NT + tid] = k;
+        }
+      }
+    if (!whole) {
+      // the CTA that finishes the last piece of the tile merges it (no wait)
+      const int64_t ua = (int64_t)tile * g.T;
+      const int64_t npieces = (((ua + g.T) * G + W - 1) / W - 1) - (((ua + 1) * G + W - 1) / W - 1) + 1;
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) {
+        const uint32_t prev = atomicAdd(g.arrivals + tile, 1u);
+        last_piece = (prev + 1 == (uint32_t)npieces);
       }
       __syncthreads();
+      if (last_piece) {
+        __threadfence();
+        merge_tile<ALG, ARGMAX>(g, tile, G, warp, lane, tid);
+      }
     }
   }
-
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int m = m0 + row_of(warp, lane, i), n = n0 + col_of(warp, lane, j);
-      if (m < g.M && n < g.N) {
-        const int64_t off = cbase + (int64_t)m * g.scm + (int64_t)n * g.scn;
-        float v = acc[i][j];
-        if (ALG == OM_MAXMUL && v == 0.f) v = 0.f;  // zero() is +0; a -0 product never wins
-        g.C[off] = v;
-        if (ARGMAX && ((remaining >> (i * 4 + j)) & 1u)) g.argmax[off] = 0u;
-      }
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -468,25 +574,27 @@ __global__ void special_scan_kernel(ScanArgs s0, ScanArgs s1, uint32_t* flags) {
 }
 
 template <int ALG, bool ARGMAX, bool A_MC, bool B_KC>
-int launch_fast(om_backend* be, const FastArgs& fa, int64_t batch) {
+int launch_fast(om_backend* be, const FastArgs& fa, int64_t grid_ctas) {
   const size_t smem =
       ARGMAX ? sizeof(float) * (resolve_region<A_MC, B_KC>() + NE * NT) + 8 * 64 * sizeof(uint32_t)
              : sizeof(float) * 2 * TB_K * (TB_M + TB_N);
   auto kern = tropical_fast_kernel<ALG, ARGMAX, A_MC, B_KC>;
   OM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
           "cudaFuncSetAttribute");
-  dim3 grid((fa.M + TB_M - 1) / TB_M, (fa.N + TB_N - 1) / TB_N, (unsigned)batch);
-  ProfScope prof(be, ARGMAX ? "tropical_fast_argmax" : "tropical_fast");
-  kern<<<grid, NT, smem, be->stream>>>(fa);
-  note_launch();
-  return check_cuda(cudaGetLastError(), "tropical_fast launch");
+  {
+    ProfScope prof(be, ARGMAX ? "tropical_fast_argmax" : "tropical_fast");
+    kern<<<(unsigned)grid_ctas, NT, smem, be->stream>>>(fa);
+    note_launch();
+    OM_CUDA(cudaGetLastError(), "tropical_fast launch");
+  }
+  return OM_OK;
 }
 
 template <int ALG>
-int launch_fast_alg(om_backend* be, const FastArgs& fa, int64_t batch, bool amc, bool bkc) {
+int launch_fast_alg(om_backend* be, const FastArgs& fa, int64_t grid_ctas, bool amc, bool bkc) {
   const bool am = fa.argmax != nullptr;
 #define OM_FAST_CASE(X, Y, Z) \
-  if (am == X && amc == Y && bkc == Z) return launch_fast<ALG, X, Y, Z>(be, fa, batch);
+  if (am == X && amc == Y && bkc == Z) return launch_fast<ALG, X, Y, Z>(be, fa, grid_ctas);
   OM_FAST_CASE(true, true, true)
   OM_FAST_CASE(true, true, false)
   OM_FAST_CASE(true, false, true)
@@ -580,17 +688,35 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
   fa.scb = g.scb;
   fa.argmax = g.argmax;
   fa.gate = be->d_flags;
+  fa.gx = (int)((g.M + TB_M - 1) / TB_M);
+  fa.gy = (int)((g.N + TB_N - 1) / TB_N);
+  fa.tiles = (int)(fa.gx * fa.gy * g.batch);
+  // two resident CTAs per SM, each with an equal share of the units
+  const int64_t G = std::min<int64_t>(fa.tiles, 2 * (int64_t)be->num_sms);
+  const int64_t W = (int64_t)fa.tiles * fa.T;
+  fa.max_units = (int)((W + G - 1) / G + 1);
+  Scratch ws, part;
   fa.ws = nullptr;
-  Scratch ws;
+  fa.part_v = nullptr;
+  fa.part_k = nullptr;
   if (g.argmax) {
-    const size_t ctas = (size_t)((g.M + TB_M - 1) / TB_M) * ((g.N + TB_N - 1) / TB_N) * g.batch;
-    OM_TRY(ws.alloc(be, ctas * (size_t)fa.T * NT * sizeof(uint32_t)));
+    OM_TRY(ws.alloc(be, (size_t)G * fa.max_units * NT * sizeof(uint32_t)));
     fa.ws = (uint32_t*)ws.ptr;
   }
+  fa.arrivals = nullptr;
+  if (G < fa.tiles || W % G != 0) {
+    const size_t pv = (size_t)G * 2 * NE * NT;
+    OM_TRY(part.alloc(be, pv * (sizeof(float) + sizeof(uint32_t)) + (size_t)fa.tiles * sizeof(uint32_t)));
+    fa.part_v = (float*)part.ptr;
+    fa.part_k = (uint32_t*)(fa.part_v + pv);
+    fa.arrivals = fa.part_k + pv;
+    OM_CUDA(cudaMemsetAsync(fa.arrivals, 0, (size_t)fa.tiles * sizeof(uint32_t), be->stream),
+            "arrival counters");
+  }
   switch (g.alg) {
-    case OM_MAXPLUS: OM_TRY(launch_fast_alg<OM_MAXPLUS>(be, fa, g.batch, amc, bkc)); break;
-    case OM_MINPLUS: OM_TRY(launch_fast_alg<OM_MINPLUS>(be, fa, g.batch, amc, bkc)); break;
-    case OM_MAXMUL: OM_TRY(launch_fast_alg<OM_MAXMUL>(be, fa, g.batch, amc, bkc)); break;
+    case OM_MAXPLUS: OM_TRY(launch_fast_alg<OM_MAXPLUS>(be, fa, G, amc, bkc)); break;
+    case OM_MINPLUS: OM_TRY(launch_fast_alg<OM_MINPLUS>(be, fa, G, amc, bkc)); break;
+    case OM_MAXMUL: OM_TRY(launch_fast_alg<OM_MAXMUL>(be, fa, G, amc, bkc)); break;
     default: return OM_OK;
   }
   GemmArgs gated = g;
@@ -754,10 +880,18 @@ extern "C" int om_b200_tropical_matmul_argmax_noalloc(void* stream, om_algebra a
   fa.argmax = argmax;
   fa.gate = sym.flag;
   fa.ws = sym.masks;
+  // one CTA per tile: no tile is cut, so no partial buffers are needed
+  fa.gx = (int)gx;
+  fa.gy = (int)gy;
+  fa.tiles = (int)(gx * gy);
+  fa.max_units = (int)T;
+  fa.part_v = nullptr;
+  fa.part_k = nullptr;
+  fa.arrivals = nullptr;
   switch (alg) {
-    case OM_MAXPLUS: OM_TRY((launch_fast<OM_MAXPLUS, true, true, true>(&view, fa, 1))); break;
-    case OM_MINPLUS: OM_TRY((launch_fast<OM_MINPLUS, true, true, true>(&view, fa, 1))); break;
-    default: OM_TRY((launch_fast<OM_MAXMUL, true, true, true>(&view, fa, 1))); break;
+    case OM_MAXPLUS: OM_TRY((launch_fast<OM_MAXPLUS, true, true, true>(&view, fa, fa.tiles))); break;
+    case OM_MINPLUS: OM_TRY((launch_fast<OM_MINPLUS, true, true, true>(&view, fa, fa.tiles))); break;
+    default: OM_TRY((launch_fast<OM_MAXMUL, true, true, true>(&view, fa, fa.tiles))); break;
   }
   GemmArgs gated = g;
   gated.fast_gate = sym.flag;
