@@ -15,16 +15,17 @@
 //                      padded).  This is also the operand gather (K1) fused
 //                      with the split, staged through a 32 x 32 shared tile so
 //                      reads and writes stay coalesced.
-//   gemm_tf32x3_kernel one CTA per 128 x 128 output tile, 192 threads:
-//                      warp 0 issues TMA loads (cp.async.bulk.tensor, 128-byte
-//                      swizzle, no multicast) of the four 128 x 32 slabs
-//                      (A_hi, A_lo, B_hi, B_lo) into a 3-stage ring with
-//                      full / empty mbarriers; warp 1 allocates 128 TMEM
-//                      columns and one thread issues 12 tcgen05.mma kind::tf32
-//                      (M = N = 128, K = 8) per slab, committing each stage
-//                      back to the producer; warps 2..5 wait for the final
-//                      commit and move the f32 accumulator out with
-//                      tcgen05.ld.32x32b (warp w reads TMEM lanes 32*(w%4)..).
+//   gemm_tf32x3_kernel persistent (one CTA per SM, tiles of 128 x 128 taken
+//                      round robin), 192 threads: warp 0 issues TMA loads
+//                      (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
+//                      of the four 128 x 32 slabs (A_hi, A_lo, B_hi, B_lo)
+//                      into a 3-stage ring with full / empty mbarriers; warp 1
+//                      allocates 2 x 128 TMEM columns and one thread issues 12
+//                      tcgen05.mma kind::tf32 (M = N = 128, K = 8) per slab,
+//                      committing each stage back to the producer; warps 2..5
+//                      move a finished accumulator out with tcgen05.ld.32x32b
+//                      (warp w reads TMEM lanes 32*(w%4)..) while the MMAs of
+//                      the next tile fill the other accumulator.
 // Every mbarrier wait is bounded; on expiry the kernel records an error word
 // that om_b200_sync reports, and every warp leaves after its own bounded
 // waits so that TMEM is always freed.
@@ -96,7 +97,7 @@ __global__ void split_tf32_kernel(SplitArgs a, int64_t tiles_k, int64_t tiles_r,
 // tcgen05 GEMM
 // ---------------------------------------------------------------------------
 struct Tf32Args {
-  int M, N, T;
+  int M, N, T, batch;
   float* C;
   int64_t scm, scn, scb;
   uint32_t* err;
@@ -153,22 +154,31 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Persistent: CTA c takes tiles c, c + G, c + 2G, ...; all roles walk the same
+// sequence.  Two 128-column TMEM accumulators alternate between tiles so the
+// epilogue of tile i overlaps the MMAs of tile i + 1.
 __global__ void __launch_bounds__(NTH, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap ahi, const __grid_constant__ CUtensorMap alo,
                        const __grid_constant__ CUtensorMap bhi, const __grid_constant__ CUtensorMap blo,
                        Tf32Args g) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accum;
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
   __shared__ uint32_t tmem_base;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN, bt = blockIdx.z;
+  const int gx = (g.M + TM - 1) / TM, gy = (g.N + TN - 1) / TN;
+  const int tiles = gx * gy * g.batch;
+  const int G = gridDim.x;
 
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&tmem_base)),
-                 "r"(TN));
+                 "r"(2 * TN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
@@ -176,7 +186,10 @@ __global__ void __launch_bounds__(NTH, 1)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[s])));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&empty[s])));
     }
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&accum)));
+    for (int b = 0; b < 2; ++b) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&tfull[b])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(smem_u32(&tempty[b])));
+    }
     asm volatile("fence.mbarrier_init.release.cluster;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -187,56 +200,72 @@ __global__ void __launch_bounds__(NTH, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
-      for (int t = 0; t < g.T && ok; ++t) {
-        const int s = t % STAGES;
-        if (t >= STAGES) ok = mbar_wait(smem_u32(&empty[s]), ((t / STAGES) - 1) & 1);
-        if (!ok) break;
-        const uint32_t bar = smem_u32(&full[s]);
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                     "r"(STAGE_BYTES)
-                     : "memory");
-        const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
-        tma_load_3d(dst, &ahi, t * TK, m0, bt, bar);
-        tma_load_3d(dst + SLAB_BYTES, &alo, t * TK, m0, bt, bar);
-        tma_load_3d(dst + 2 * SLAB_BYTES, &bhi, t * TK, n0, bt, bar);
-        tma_load_3d(dst + 3 * SLAB_BYTES, &blo, t * TK, n0, bt, bar);
+      int q = 0;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += G) {
+        const int bx = tile % gx, by = (tile / gx) % gy, bt = tile / (gx * gy);
+        for (int t = 0; t < g.T && ok; ++t, ++q) {
+          const int s = q % STAGES;
+          if (q >= STAGES) ok = mbar_wait(smem_u32(&empty[s]), ((q / STAGES) - 1) & 1);
+          if (!ok) break;
+          const uint32_t bar = smem_u32(&full[s]);
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                       "r"(STAGE_BYTES)
+                       : "memory");
+          const uint32_t dst = smem_u32(smem + s * STAGE_BYTES);
+          tma_load_3d(dst, &ahi, t * TK, bx * TM, bt, bar);
+          tma_load_3d(dst + SLAB_BYTES, &alo, t * TK, bx * TM, bt, bar);
+          tma_load_3d(dst + 2 * SLAB_BYTES, &bhi, t * TK, by * TN, bt, bar);
+          tma_load_3d(dst + 3 * SLAB_BYTES, &blo, t * TK, by * TN, bt, bar);
+        }
       }
       if (!ok) atomicOr(g.err, 1u);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
-      for (int t = 0; t < g.T && ok; ++t) {
-        const int s = t % STAGES;
-        ok = mbar_wait(smem_u32(&full[s]), (t / STAGES) & 1);
+      int q = 0, i = 0;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += G, ++i) {
+        const int ab = i & 1;
+        if (i >= 2) ok = mbar_wait(smem_u32(&tempty[ab]), ((i >> 1) - 1) & 1);
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;");
-        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t d = tmem + (uint32_t)(ab * TN);
+        for (int t = 0; t < g.T && ok; ++t, ++q) {
+          const int s = q % STAGES;
+          ok = mbar_wait(smem_u32(&full[s]), (q / STAGES) & 1);
+          if (!ok) break;
+          asm volatile("tcgen05.fence::after_thread_sync;");
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
-        for (int j = 0; j < TK / 8; ++j) {
-          const uint64_t a_h = sw128_desc(base + j * 32);
-          const uint64_t a_l = sw128_desc(base + SLAB_BYTES + j * 32);
-          const uint64_t b_h = sw128_desc(base + 2 * SLAB_BYTES + j * 32);
-          const uint64_t b_l = sw128_desc(base + 3 * SLAB_BYTES + j * 32);
-          mma_tf32(tmem, a_l, b_h, (t > 0 || j > 0) ? 1u : 0u);
-          mma_tf32(tmem, a_h, b_l, 1u);
-          mma_tf32(tmem, a_h, b_h, 1u);
+          for (int j = 0; j < TK / 8; ++j) {
+            const uint64_t a_h = sw128_desc(base + j * 32);
+            const uint64_t a_l = sw128_desc(base + SLAB_BYTES + j * 32);
+            const uint64_t b_h = sw128_desc(base + 2 * SLAB_BYTES + j * 32);
+            const uint64_t b_l = sw128_desc(base + 3 * SLAB_BYTES + j * 32);
+            mma_tf32(d, a_l, b_h, (t > 0 || j > 0) ? 1u : 0u);
+            mma_tf32(d, a_h, b_l, 1u);
+            mma_tf32(d, a_h, b_h, 1u);
+          }
+          mma_commit(smem_u32(&empty[s]));
         }
-        mma_commit(smem_u32(&empty[s]));
+        mma_commit(smem_u32(&tfull[ab]));  // fires when this tile's MMAs are done
       }
-      mma_commit(smem_u32(&accum));  // fires once every issued MMA has completed
       if (!ok) atomicOr(g.err, 1u);
     }
-  } else {  // epilogue warps 2..5
-    ok = mbar_wait(smem_u32(&accum), 0);
-    asm volatile("tcgen05.fence::after_thread_sync;");
-    if (ok) {
-      const int quad = warp & 3;
-      const int m = m0 + 32 * quad + lane;
+  } else {  // epilogue warps 2..5: TMEM lanes 32*(warp % 4)
+    const int quad = warp & 3;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += G, ++i) {
+      const int ab = i & 1;
+      ok = mbar_wait(smem_u32(&tfull[ab]), (i >> 1) & 1);
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      const int bx = tile % gx, by = (tile / gx) % gy, bt = tile / (gx * gy);
+      const int m = bx * TM + 32 * quad + lane;
       float* Cb = g.C + (int64_t)bt * g.scb;
 #pragma unroll 1
       for (int c0 = 0; c0 < TN; c0 += 32) {
         uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)c0;
+        const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(ab * TN + c0);
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
             "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -250,20 +279,24 @@ __global__ void __launch_bounds__(NTH, 1)
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         if (m < g.M) {
 #pragma unroll
-          for (int q = 0; q < 32; ++q) {
-            const int n = n0 + c0 + q;
-            if (n < g.N) Cb[(int64_t)m * g.scm + (int64_t)n * g.scn] = __uint_as_float(r[q]);
+          for (int qq = 0; qq < 32; ++qq) {
+            const int n = by * TN + c0 + qq;
+            if (n < g.N) Cb[(int64_t)m * g.scm + (int64_t)n * g.scn] = __uint_as_float(r[qq]);
           }
         }
       }
-    } else if (lane == 0) {
-      atomicOr(g.err, 1u);
+      // hand the accumulator back to the MMA issuer
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[ab]));
     }
+    if (!ok && lane == 0) atomicOr(g.err, 1u);
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(2 * TN));
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -345,7 +378,10 @@ int launch_gemm_tf32(om_backend* be, const GemmArgs& g, bool* handled) {
   OM_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem),
           "cudaFuncSetAttribute(tf32)");
-  dim3 grid((a.M + TM - 1) / TM, (a.N + TN - 1) / TN, (unsigned)g.batch);
+  a.batch = (int)g.batch;
+  const int64_t tiles = (int64_t)((a.M + TM - 1) / TM) * ((a.N + TN - 1) / TN) * g.batch;
+  if (tiles > (1ll << 31) - 1) return OM_OK;
+  const unsigned grid = (unsigned)std::min<int64_t>(tiles, be->num_sms);
   {
     ProfScope prof(be, "gemm_tf32x3_tcgen05");
     gemm_tf32x3_kernel<<<grid, NTH, smem, be->stream>>>(m_ahi, m_alo, m_bhi, m_blo, a);
