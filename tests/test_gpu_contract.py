@@ -269,3 +269,25 @@ def test_headline_2048_maxplus_argmax(be):
     jj = np.arange(n)[None, :]
     attained = (Am[np.arange(m)[:, None], AM] + Bm[AM, jj]).astype(np.float32)
     assert bits_equal(attained, C)
+
+
+@pytest.mark.parametrize("shape", [(3, 200, 72, 96), (2, 130, 33, 257), (4, 64, 1000, 64)],
+                         ids=["b3", "ragged", "deepk"])
+def test_standard_f32_tensor_core_batched(be, shape):
+    # 'bij,bjk->bik' with batch first (non-contiguous batch stride) through the
+    # tcgen05 3xTF32 path; checked with the GEMM error bound
+    bsz, m, k, n = shape
+    sa, sb = [bsz, m, k], [bsz, k, n]
+    a = orc.normal(91, bsz * m * k)
+    b = orc.normal(92, bsz * k * n)
+    check_case(be, "standard", a, sa, col(sa), [0, 1, 2], b, sb, col(sb), [0, 2, 3],
+               [bsz, m, n], [0, 1, 3], argmax=False)
+
+
+def test_standard_f32_tensor_core_padded_views(be):
+    # sub-matrix views with padded leading dimensions, output transposed
+    m, k, n, lda, ldb = 200, 150, 180, 208, 160
+    a = orc.normal(93, lda * k)
+    b = orc.normal(94, ldb * n)
+    check_case(be, "standard", a, [m, k], [1, lda], [0, 1], b, [k, n], [1, ldb], [1, 2], [n, m],
+               [2, 0], argmax=False)
