@@ -48,7 +48,7 @@ FP32_PEAK_TOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 PAIR_CEILING_TOPS = 148 * 39 * 4 * 1.965e9 / 1e12
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
 # kernel, from the ncu capture summarised in profiles/.
-NCU_TRAFFIC_BYTES = 34874880 + 21393408  # profiles/tropical_fast_maxplus_2048_ncu.md
+NCU_TRAFFIC_BYTES = 47254016 + 50772992  # profiles/tropical_fast_maxplus_2048_ncu.md
 
 
 def load_pkg():
@@ -400,12 +400,38 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-check", action="store_true")
+    ap.add_argument("--case", default="headline", choices=["headline", "config2", "contract"],
+                    help="profiling cases: config2 = only the config-2 permuted "
+                         "contraction; contract = only warmup + steps headline calls")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.case == "config2":
+        import torch
+        om = load_pkg()
+        torch.cuda.set_device(local_rank)
+        be = om.B200(local_rank)
+        print(json.dumps(run_permuted(be, om, local_rank)), flush=True)
+        be.close()
+        return
+    if args.case == "contract":
+        import torch
+        om = load_pkg()
+        torch.cuda.set_device(local_rank)
+        be = om.B200(local_rank)
+        a, b = inputs()
+        A, B = be.from_slice(a), be.from_slice(b)
+        C, AM = be.alloc(M * N, np.float32), be.alloc(M * N, np.uint32)
+        for _ in range(args.warmup + args.steps):
+            be.contract_into("maxplus", A, [M, K], [1, M], [0, 1], B, [K, N], [1, K], [1, 2],
+                             [M, N], [0, 2], C, AM)
+        be.synchronize()
+        print(json.dumps({"case": "contract", "calls": args.warmup + args.steps}), flush=True)
+        be.close()
         return
     if world > 1:
         import torch
