@@ -400,9 +400,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-check", action="store_true")
-    ap.add_argument("--case", default="headline", choices=["headline", "config2", "contract"],
+    ap.add_argument("--case", default="headline", choices=["headline", "config2", "contract", "network"],
                     help="profiling cases: config2 = only the config-2 permuted "
-                         "contraction; contract = only warmup + steps headline calls")
+                         "contraction; contract = only warmup + steps headline calls; "
+                         "network = only the sliced MIS network, with its kernel breakdown")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -416,6 +417,20 @@ def main():
         torch.cuda.set_device(local_rank)
         be = om.B200(local_rank)
         print(json.dumps(run_permuted(be, om, local_rank)), flush=True)
+        be.close()
+        return
+    if args.case == "network" and world == 1:
+        import torch
+        om = load_pkg()
+        torch.cuda.set_device(local_rank)
+        be = om.B200(local_rank)
+        be.profile(True)
+        net = run_network(be, om, 1, 0, local_rank, args)
+        prof = be.profile_report()
+        be.profile(False)
+        net["kernels_ms_total"] = {k: [round(v[0], 3), v[1]] for k, v in
+                                   sorted(prof.items(), key=lambda kv: -kv[1][0])}
+        print(json.dumps(net), flush=True)
         be.close()
         return
     if args.case == "contract":

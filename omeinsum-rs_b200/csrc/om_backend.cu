@@ -7,6 +7,7 @@
 // release threshold, so freed blocks are cached and reused without a device
 // synchronisation -- the device-side counterpart of the CPU ScratchPool
 // (src/backend/cpu/buffer_pool.rs:2-47).
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -30,6 +31,14 @@ int check_cuda(cudaError_t e, const char* what) {
 }
 
 void note_launch(int n) { g_launches += n; }
+
+bool trace_on() {
+  static const bool on = [] {
+    const char* v = std::getenv("OM_B200_TRACE");
+    return v && v[0] && v[0] != '0';
+  }();
+  return on;
+}
 
 ProfScope::ProfScope(om_backend* b, const char* name) : be(b) {
   if (!be || !be->profiling) return;

@@ -17,6 +17,7 @@
 // output whose groups cannot be flattened goes through a scratch buffer and a
 // permuting gather.
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <set>
 #include <string>
@@ -138,6 +139,77 @@ uint64_t zero_pattern(om_algebra alg, om_dtype dt) {
   return u;
 }
 
+// Plans gemm_node: output modes in C's memory order (C is contiguous), the
+// contracted ones in `contr` order; adjacent modes contiguous in both A and
+// B merge.  False when the node exceeds the kernel's limits.
+bool plan_node(const Operand& A, const Operand& B, const Operand& C,
+               const std::vector<int32_t>& contr, NodeArgs& g);
+bool node_fits(const Operand& A, const Operand& B, const Operand& C,
+               const std::vector<int32_t>& contr) {
+  NodeArgs g;
+  return plan_node(A, B, C, contr, g);
+}
+
+bool plan_node(const Operand& A, const Operand& B, const Operand& C,
+               const std::vector<int32_t>& contr, NodeArgs& g) {
+  struct M3 {
+    int64_t ext, sa, sb;
+  };
+  auto stride_in = [](const Operand& op, int32_t m) -> int64_t {
+    int p = op.pos(m);
+    return p >= 0 ? op.strides[p] : 0;
+  };
+  auto build = [&](const std::vector<int32_t>& modes, const Operand& ref, std::vector<M3>& out) {
+    for (int32_t m : modes) {
+      const int64_t e = ref.shape[ref.pos(m)];
+      if (e == 1) continue;
+      const int64_t sa = stride_in(A, m), sb = stride_in(B, m);
+      if (!out.empty() && out.back().sa * out.back().ext == sa &&
+          out.back().sb * out.back().ext == sb && out.back().ext * e < (int64_t(1) << 32)) {
+        out.back().ext *= e;
+        continue;
+      }
+      out.push_back({e, sa, sb});
+    }
+  };
+  std::vector<M3> om, km;
+  build(C.modes, C, om);
+  build(contr, A, km);
+  // split a long leading mode so that the tile has a row of several blocks
+  if (!om.empty() && om[0].ext > 1024 && om[0].ext % 256 == 0) {
+    M3 rest{om[0].ext / 256, om[0].sa * 256, om[0].sb * 256};
+    om[0].ext = 256;
+    om.insert(om.begin() + 1, rest);
+  }
+  if (om.size() > (size_t)kMaxNodeModes || km.size() > (size_t)kMaxNodeModes) return false;
+  int64_t total = 1, K = 1;
+  for (auto& x : om) {
+    if (x.ext >= (int64_t(1) << 32)) return false;
+    total *= x.ext;
+  }
+  for (auto& x : km) {
+    if (x.ext >= (int64_t(1) << 32)) return false;
+    K *= x.ext;
+  }
+  int nlow = 0;
+  int64_t P = 1;
+  while (nlow < (int)om.size() && P * om[nlow].ext <= 1024) P *= om[nlow++].ext;
+  if (K >= (int64_t(1) << 32) || total / P >= (int64_t(1) << 32)) return false;
+  g = NodeArgs{};
+  g.K = K;
+  g.total = total;
+  g.P = (int32_t)P;
+  g.rows = total / P;
+  g.nlow = nlow;
+  g.nout = (int)om.size();
+  g.nk = (int)km.size();
+  for (size_t j = 0; j < om.size(); ++j)
+    g.out[j] = NodeMode{make_fastdiv((uint32_t)om[j].ext), om[j].sa, om[j].sb};
+  for (size_t j = 0; j < km.size(); ++j)
+    g.kmodes[j] = NodeMode{make_fastdiv((uint32_t)km[j].ext), km[j].sa, km[j].sb};
+  return true;
+}
+
 }  // namespace
 
 int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Operand A,
@@ -230,50 +302,94 @@ int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Op
   rfree = choose_order(rfree, {&B, &C}, false);
   batch = choose_order(batch, {&A, &B, &C}, false);
 
-  // Small, batched shapes (tensor-network nodes) whose operands or output do
-  // not flatten are contracted in place by decoding every mode, instead of
-  // gathering: for these memory-bound nodes the gathers would cost more than
-  // the contraction itself.
+  Scratch node_a, node_b;
+  // Small or heavily batched shapes (tensor-network nodes) whose operands do
+  // not flatten are contracted in place (gemm_node) instead of gathered: for
+  // these memory-bound nodes a gather would cost as much as the contraction.
   {
     const int64_t M0 = group_size(A, lfree), N0 = group_size(B, rfree);
-    // thread per output: the shapes the small GEMM kernel takes anyway
-    const bool small = (M0 * N0 <= 1024) || M0 < 16 || N0 < 16;
+    const int64_t K0 = group_size(A, contr);
+    const bool small = (M0 * N0 <= 1024) || M0 < 16 || N0 < 16 || K0 <= 8;
     const bool flat = flat_stride(A, lfree) >= 0 && flat_stride(A, contr) >= 0 &&
                       flat_stride(A, batch) >= 0 && flat_stride(B, contr) >= 0 &&
                       flat_stride(B, rfree) >= 0 && flat_stride(B, batch) >= 0 &&
                       flat_stride(C, lfree) >= 0 && flat_stride(C, rfree) >= 0 &&
                       flat_stride(C, batch) >= 0;
-    const bool fits = lfree.size() <= (size_t)kMaxGroupModes && rfree.size() <= (size_t)kMaxGroupModes &&
-                      contr.size() <= (size_t)kMaxGroupModes && batch.size() <= (size_t)kMaxGroupModes;
-    if (small && !flat && fits) {
-      StridedGemmArgs sg{};
-      sg.alg = alg;
-      sg.dtype = dt;
-      sg.M = M0;
-      sg.N = N0;
-      sg.K = group_size(A, contr);
-      sg.batch = group_size(A, batch);
-      sg.A = a;
-      sg.B = b;
-      sg.C = c_out;
-      sg.argmax = argmax;
-      auto fill = [&](ModeGroup& grp, const std::vector<int32_t>& modes, const Operand* o0,
-                      const Operand* o1, const Operand* o2) {
-        grp.n = (int)modes.size();
-        for (size_t j = 0; j < modes.size(); ++j) {
-          const int32_t md = modes[j];
-          const Operand* ref = o0->pos(md) >= 0 ? o0 : o1;
-          grp.ext[j] = ref->shape[ref->pos(md)];
-          grp.s0[j] = o0 ? o0->strides[o0->pos(md)] : 0;
-          grp.s1[j] = o1 ? o1->strides[o1->pos(md)] : 0;
-          grp.s2[j] = o2 ? o2->strides[o2->pos(md)] : 0;
+    if (trace_on())
+      fprintf(stderr, "[om trace] contract alg=%d M=%lld N=%lld K=%lld batch=%lld flat=%d small=%d argmax=%d\n",
+              (int)alg, (long long)M0, (long long)N0, (long long)K0,
+              (long long)group_size(A, batch), (int)flat, (int)small, (int)track);
+    // The node kernel's reads coalesce when C's leading modes (8 outputs)
+    // are, together with the operand's contracted modes, the operand's
+    // densest modes.  An operand that is not laid out so is first gathered
+    // into C's mode order (contracted modes last); for the small operand of
+    // a node this costs little, for a large one it replaces scattered reads
+    // by one streaming permutation.
+    auto aligned = [&](const Operand& X) {
+      std::vector<int32_t> lead;
+      int64_t prod = 1;
+      for (size_t i = 0; i < C.modes.size() && prod < 8; ++i)
+        if (C.shape[i] > 1) {
+          lead.push_back(C.modes[i]);
+          prod *= C.shape[i];
         }
+      auto in = [](const std::vector<int32_t>& v, int32_t m) {
+        return std::find(v.begin(), v.end(), m) != v.end();
       };
-      fill(sg.gm, lfree, &A, &C, nullptr);
-      fill(sg.gn, rfree, &B, &C, nullptr);
-      fill(sg.gk, contr, &A, &B, nullptr);
-      fill(sg.gb, batch, &A, &B, &C);
-      return launch_gemm_small_strided(be, sg);
+      int remaining = 0;
+      for (int32_t m : lead) remaining += X.pos(m) >= 0;
+      std::vector<int> idx;
+      for (size_t i = 0; i < X.modes.size(); ++i)
+        if (X.shape[i] > 1) idx.push_back((int)i);
+      std::stable_sort(idx.begin(), idx.end(),
+                       [&](int x, int y) { return X.strides[x] < X.strides[y]; });
+      int64_t expect = 1;
+      for (int i : idx) {
+        if (remaining == 0) break;
+        if (X.strides[i] != expect) return false;
+        const bool l = in(lead, X.modes[i]);
+        if (!l && !in(contr, X.modes[i])) return false;
+        remaining -= l;
+        expect *= X.shape[i];
+      }
+      return true;
+    };
+    auto align = [&](const void*& ptr, Operand& X, Scratch& buf) -> int {
+      if (aligned(X)) return OM_OK;
+      std::vector<int32_t> cm, none;
+      for (int32_t m : C.modes)
+        if (X.pos(m) >= 0) cm.push_back(m);
+      Operand g;
+      OM_TRY(gather_operand(be, es, ptr, X, cm, contr, none, buf, g));
+      ptr = buf.ptr;
+      X = g;
+      return OM_OK;
+    };
+    if (small && !flat && node_fits(A, B, C, contr)) {
+      OM_TRY(align(a, A, node_a));
+      OM_TRY(align(b, B, node_b));
+    }
+    NodeArgs na;
+    if (small && !flat && plan_node(A, B, C, contr, na)) {
+      na.alg = alg;
+      na.dtype = dt;
+      na.A = a;
+      na.B = b;
+      na.C = c_out;
+      na.argmax = argmax;
+      if (trace_on()) {
+        fprintf(stderr, "[om trace] node total=%lld K=%lld P=%d nlow=%d out=", (long long)na.total,
+                (long long)na.K, na.P, na.nlow);
+        for (int j = 0; j < na.nout; ++j)
+          fprintf(stderr, "%s%u:%lld:%lld", j ? "," : "", na.out[j].div.d, (long long)na.out[j].sa,
+                  (long long)na.out[j].sb);
+        fprintf(stderr, " k=");
+        for (int j = 0; j < na.nk; ++j)
+          fprintf(stderr, "%s%u:%lld:%lld", j ? "," : "", na.kmodes[j].div.d,
+                  (long long)na.kmodes[j].sa, (long long)na.kmodes[j].sb);
+        fprintf(stderr, "\n");
+      }
+      return launch_gemm_node(be, na);
     }
   }
 

@@ -12,11 +12,13 @@
 //                        tropical unary  -> tropical_unary_backward (:213-238),
 //                        Standard binary -> two contractions (:287-332),
 //                        Standard unary  -> index exchange (:183-195).
-// Every binary node writes its output in native order (free labels of the
-// left operand, free labels of the right one, batch labels), as the
+// A GEMM-shaped binary node writes its output in native order (free labels
+// of the left operand, free labels of the right one, batch labels), as the
 // reference's value path does (contract_binary_native_order, ops.rs:122-143),
-// so the GEMM writes without a permutation; the root is finalised to iy.  The
-// tape keys every gradient by label, so this order changes no result.
+// so the GEMM writes without a permutation; a node small or batched enough
+// to run thread-per-output writes in its larger operand's memory order
+// instead (node_order); the root is finalised to iy.  The tape keys every
+// gradient by label, so these orders change no result.
 #include <algorithm>
 #include <map>
 #include <memory>
@@ -183,6 +185,43 @@ struct Engine {
     for (auto l : ia)
       if (has(iy, l) && has(ib, l) && !has(r, l)) r.push_back(l);
     return r.size() == iy.size() ? r : iy;
+  }
+
+  // Output order of a node that runs as a thread-per-output contraction
+  // (small M*N, M or N below 16, or k of at most 8): the free and batch
+  // labels of the larger operand in its memory order, then the rest in the
+  // other operand's memory order.  The node then streams its larger input
+  // and its output in the same order, both coalesced, and the next node
+  // inherits the layout.  Larger nodes keep native_order (the GEMM's).
+  std::vector<int32_t> node_order(const DTensor& a, const DTensor& b,
+                                  const std::vector<int32_t>& iy) const {
+    auto pos = [](const std::vector<int32_t>& v, int32_t l) -> int {
+      for (size_t i = 0; i < v.size(); ++i)
+        if (v[i] == l) return (int)i;
+      return -1;
+    };
+    int64_t M = 1, N = 1, K = 1;
+    for (size_t i = 0; i < a.ix.size(); ++i) {
+      const bool inb = pos(b.ix, a.ix[i]) >= 0, iny = pos(iy, a.ix[i]) >= 0;
+      if (iny && !inb) M *= a.shape[i];
+      if (inb && !iny) K *= a.shape[i];
+    }
+    for (size_t i = 0; i < b.ix.size(); ++i)
+      if (pos(iy, b.ix[i]) >= 0 && pos(a.ix, b.ix[i]) < 0) N *= b.shape[i];
+    const bool small = M * N <= 1024 || M < 16 || N < 16 || K <= 8;
+    if (!small) return native_order(a.ix, b.ix, iy);
+    const DTensor& big = a.numel() >= b.numel() ? a : b;
+    const DTensor& other = &big == &a ? b : a;
+    std::vector<int32_t> r;
+    for (const DTensor* t : {&big, &other}) {
+      std::vector<int> idx;
+      for (size_t i = 0; i < t->ix.size(); ++i)
+        if (pos(iy, t->ix[i]) >= 0 && pos(r, t->ix[i]) < 0) idx.push_back((int)i);
+      std::stable_sort(idx.begin(), idx.end(),
+                       [&](int x, int y) { return t->strides[x] < t->strides[y]; });
+      for (int i : idx) r.push_back(t->ix[i]);
+    }
+    return r.size() == iy.size() ? r : native_order(a.ix, b.ix, iy);
   }
 
   int push_unary(int child, const std::vector<int32_t>& oix, int* out_node) {
@@ -356,7 +395,7 @@ extern "C" int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, in
       n.child1 = r;
       n.left_ix = lix;
       n.right_ix = E.nodes[r].content.ix;
-      n.out_ix = Engine::native_order(n.left_ix, n.right_ix, niy_);
+      n.out_ix = E.node_order(E.nodes[l].content, E.nodes[r].content, niy_);
       OM_TRY(E.contract(E.nodes[l].content, n.left_ix, E.nodes[r].content, n.right_ix, n.out_ix,
                         E.keep && E.tropical, n.content, n.argmax));
       E.nodes.push_back(std::move(n));

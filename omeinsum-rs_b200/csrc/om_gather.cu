@@ -8,6 +8,7 @@
 // 32x32 tile in shared memory when the source's unit-stride axis is not the
 // destination's first axis.
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <vector>
 
@@ -107,6 +108,210 @@ __global__ void gather_transpose(const T* __restrict__ src, T* __restrict__ dst,
   }
 }
 
+// Permutation of a dense source (its axes, sorted by stride, form a
+// column-major layout) where no single axis is long enough for the row or
+// 32x32-transpose paths -- e.g. a network intermediate of many extent-2
+// modes.  A tile is the product of a set U of axes holding at least 32
+// elements contiguous in the source and at least 32 contiguous in the
+// destination; the remaining axes R index tiles.  Three per-CTA tables
+// (built once) give the source offset of each tile element in source order,
+// its slot in the tile (destination order) and its destination offset, so
+// both global sides move in runs of >= 32 elements and the per-element index
+// work is two shared-memory reads.  Each CTA walks a contiguous range of
+// tiles with an odometer over R, so tile bases cost O(1) per tile.
+constexpr int kPermMaxTile = 2048;
+
+struct PermDesc {
+  int nu, nr;
+  int32_t t;                        // tile size = prod of U extents
+  int32_t u_shape[OM_MAX_DIMS];     // U in destination order
+  int32_t u_sstr[OM_MAX_DIMS];      // source stride of each U axis
+  int32_t u_dstr[OM_MAX_DIMS];      // destination stride of each U axis
+  int32_t u_tpos[OM_MAX_DIMS];      // stride of each U axis inside the tile
+  int32_t us_order[OM_MAX_DIMS];    // U indices sorted by source stride
+  int64_t r_shape[OM_MAX_DIMS];     // R in destination order
+  int64_t r_sstr[OM_MAX_DIMS];
+  int64_t r_dstr[OM_MAX_DIMS];
+  int64_t ntiles;
+};
+
+__device__ __forceinline__ int perm_pad(int j) { return j + (j >> 5); }
+
+template <typename T>
+__global__ void __launch_bounds__(256) gather_perm_tiled(const T* __restrict__ src,
+                                                         T* __restrict__ dst, PermDesc p) {
+  extern __shared__ __align__(16) unsigned char perm_smem[];
+  int32_t* s_src = reinterpret_cast<int32_t*>(perm_smem);  // by source order
+  int32_t* s_slot = s_src + p.t;                             // by source order
+  int32_t* s_dst = s_slot + p.t;                             // by tile slot
+  int64_t* s_base = reinterpret_cast<int64_t*>(s_dst + p.t + (p.t & 1));  // [2][2]
+  int64_t* s_coord = s_base + 4;                                           // [nr]
+  T* tile = reinterpret_cast<T*>(s_coord + OM_MAX_DIMS);
+  const int tid = threadIdx.x, nth = blockDim.x;
+
+  for (int j = tid; j < p.t; j += nth) {
+    int rem = j, doff = 0;
+    for (int u = 0; u < p.nu; ++u) {
+      int c = rem % p.u_shape[u];
+      rem /= p.u_shape[u];
+      doff += c * p.u_dstr[u];
+    }
+    s_dst[j] = doff;
+    // j read as an index in source order
+    rem = j;
+    int soff = 0, slot = 0;
+    for (int q = 0; q < p.nu; ++q) {
+      int u = p.us_order[q];
+      int c = rem % p.u_shape[u];
+      rem /= p.u_shape[u];
+      soff += c * p.u_sstr[u];
+      slot += c * p.u_tpos[u];
+    }
+    s_src[j] = soff;
+    s_slot[j] = slot;
+  }
+  const int64_t per = (p.ntiles + gridDim.x - 1) / gridDim.x;
+  const int64_t o0 = blockIdx.x * per;
+  const int64_t o1 = o0 + per < p.ntiles ? o0 + per : p.ntiles;
+  if (tid == 0) {
+    int64_t rem = o0, sb = 0, db = 0;
+    for (int r = 0; r < p.nr; ++r) {
+      int64_t c = rem % p.r_shape[r];
+      rem /= p.r_shape[r];
+      s_coord[r] = c;
+      sb += c * p.r_sstr[r];
+      db += c * p.r_dstr[r];
+    }
+    s_base[0] = sb;
+    s_base[1] = db;
+  }
+  __syncthreads();
+  int cur = 0;
+  for (int64_t o = o0; o < o1; ++o) {
+    const int64_t sb = s_base[2 * cur], db = s_base[2 * cur + 1];
+#pragma unroll 4
+    for (int i = tid; i < p.t; i += nth) tile[perm_pad(s_slot[i])] = src[sb + s_src[i]];
+    __syncthreads();
+    if (tid == 0) {  // odometer step to tile o + 1
+      int64_t nsb = sb, ndb = db;
+      for (int r = 0; r < p.nr; ++r) {
+        int64_t c = s_coord[r] + 1;
+        if (c < p.r_shape[r]) {
+          s_coord[r] = c;
+          nsb += p.r_sstr[r];
+          ndb += p.r_dstr[r];
+          break;
+        }
+        s_coord[r] = 0;
+        nsb -= (p.r_shape[r] - 1) * p.r_sstr[r];
+        ndb -= (p.r_shape[r] - 1) * p.r_dstr[r];
+      }
+      s_base[2 * (cur ^ 1)] = nsb;
+      s_base[2 * (cur ^ 1) + 1] = ndb;
+    }
+#pragma unroll 4
+    for (int j = tid; j < p.t; j += nth) dst[db + s_dst[j]] = tile[perm_pad(j)];
+    __syncthreads();
+    cur ^= 1;
+  }
+}
+
+// Plans the tiled permutation; false when the source is not a dense
+// permutation or no tile of at most kPermMaxTile elements has 32-element
+// runs on both sides.
+bool plan_perm(const GatherDesc& d0, const int64_t* dstr0, int64_t n, PermDesc& p) {
+  if (d0.nd < 2 || n >= (int64_t(1) << 31)) return false;
+  // Split each long axis into (piece, rest) so that a tile can take a
+  // 32-element piece of it: a transpose of an extent-2 axis against a long
+  // contiguous one then still gets 128-byte runs on both sides.
+  GatherDesc d;
+  int64_t dstr[OM_MAX_DIMS];
+  d.nd = 0;
+  for (int k = 0; k < d0.nd; ++k) {
+    const int64_t e = d0.shape[k];
+    int64_t piece = 0;
+    if (e > 64)
+      for (int64_t c : {32, 64, 16, 48, 40, 24, 56, 8})
+        if (e % c == 0) {
+          piece = c;
+          break;
+        }
+    if (d.nd + (piece ? 2 : 1) > OM_MAX_DIMS) return false;
+    if (piece) {
+      d.shape[d.nd] = piece;
+      d.sstride[d.nd] = d0.sstride[k];
+      dstr[d.nd++] = dstr0[k];
+      d.shape[d.nd] = e / piece;
+      d.sstride[d.nd] = d0.sstride[k] * piece;
+      dstr[d.nd++] = dstr0[k] * piece;
+    } else {
+      d.shape[d.nd] = e;
+      d.sstride[d.nd] = d0.sstride[k];
+      dstr[d.nd++] = dstr0[k];
+    }
+  }
+  int sorder[OM_MAX_DIMS];
+  for (int k = 0; k < d.nd; ++k) sorder[k] = k;
+  std::sort(sorder, sorder + d.nd, [&](int x, int y) { return d.sstride[x] < d.sstride[y]; });
+  int64_t expect = 1;
+  for (int q = 0; q < d.nd; ++q) {
+    if (d.sstride[sorder[q]] != expect) return false;
+    expect *= d.shape[sorder[q]];
+  }
+  bool in_u[OM_MAX_DIMS] = {};
+  int64_t t = 1, run = 1;
+  for (int k = 0; k < d.nd && run < 32; ++k) {
+    in_u[k] = true;
+    t *= d.shape[k];
+    run *= d.shape[k];
+  }
+  run = 1;
+  for (int q = 0; q < d.nd && run < 32; ++q) {
+    int k = sorder[q];
+    run *= d.shape[k];
+    if (!in_u[k]) {
+      in_u[k] = true;
+      t *= d.shape[k];
+    }
+  }
+  if (t > kPermMaxTile) return false;
+  for (int k = 0; k < d.nd && t < 1024; ++k)
+    if (!in_u[k] && t * d.shape[k] <= kPermMaxTile) {
+      in_u[k] = true;
+      t *= d.shape[k];
+    }
+  p.nu = p.nr = 0;
+  p.t = (int32_t)t;
+  int32_t tp = 1;
+  for (int k = 0; k < d.nd; ++k) {
+    if (in_u[k]) {
+      p.u_shape[p.nu] = (int32_t)d.shape[k];
+      p.u_sstr[p.nu] = (int32_t)d.sstride[k];
+      p.u_dstr[p.nu] = (int32_t)dstr[k];
+      p.u_tpos[p.nu] = tp;
+      tp *= (int32_t)d.shape[k];
+      p.nu++;
+    } else {
+      p.r_shape[p.nr] = d.shape[k];
+      p.r_sstr[p.nr] = d.sstride[k];
+      p.r_dstr[p.nr] = dstr[k];
+      p.nr++;
+    }
+  }
+  for (int u = 0; u < p.nu; ++u) p.us_order[u] = u;
+  std::sort(p.us_order, p.us_order + p.nu,
+            [&](int x, int y) { return p.u_sstr[x] < p.u_sstr[y]; });
+  p.ntiles = n / t;
+  return true;
+}
+
+int perm_pad_host(int j) { return j + (j >> 5); }
+
+size_t perm_smem_bytes(const PermDesc& p, size_t es) {
+  size_t tables = 4 * (3 * (size_t)p.t + (p.t & 1));
+  return tables + 8 * (4 + OM_MAX_DIMS) + es * (size_t)perm_pad_host(p.t);
+}
+
 int grid_for(om_backend* be, int64_t work, int per_block) {
   int64_t g = (work + per_block - 1) / per_block;
   int64_t cap = (int64_t)be->num_sms * 32;
@@ -137,6 +342,16 @@ int gather_typed(om_backend* be, const T* src, T* dst, GatherDesc d, int64_t n) 
     gather_rows<T><<<grid_for(be, rows, 1), threads, 0, be->stream>>>(src, dst, d, rows);
     note_launch();
     return check_cuda(cudaGetLastError(), "gather_rows launch");
+  }
+  {
+    PermDesc pd;
+    if (plan_perm(d, dstr, n, pd)) {
+      size_t smem = perm_smem_bytes(pd, sizeof(T));  // <= 42 KB: no opt-in needed
+      int64_t g = std::min<int64_t>(pd.ntiles, (int64_t)be->num_sms * 4);
+      gather_perm_tiled<T><<<(int)g, 256, smem, be->stream>>>(src, dst, pd);
+      note_launch();
+      return check_cuda(cudaGetLastError(), "gather_perm_tiled launch");
+    }
   }
   int p = -1;
   for (int k = 1; k < d.nd; ++k)
@@ -202,6 +417,12 @@ int launch_gather(om_backend* be, size_t es, const void* src, int ndim, const in
     d.nd++;
   }
   const char* s = (const char*)src + offset * (int64_t)es;
+  if (trace_on()) {
+    fprintf(stderr, "[om trace] gather es=%zu n=%lld axes=", es, (long long)n);
+    for (int k = 0; k < d.nd; ++k)
+      fprintf(stderr, "%s%lld:%lld", k ? "," : "", (long long)d.shape[k], (long long)d.sstride[k]);
+    fprintf(stderr, "\n");
+  }
   ProfScope prof(be, "gather");
   if (es == 8) return gather_typed<uint64_t>(be, (const uint64_t*)s, (uint64_t*)dst, d, n);
   if (es == 4) return gather_typed<uint32_t>(be, (const uint32_t*)s, (uint32_t*)dst, d, n);

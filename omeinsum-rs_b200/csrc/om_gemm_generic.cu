@@ -14,6 +14,7 @@
 //               memory; for the tiny, heavily batched GEMMs of tensor-network
 //               nodes (bond dimension 2), where a tile would be mostly idle.
 #include <algorithm>
+#include <type_traits>
 
 #include "om_internal.h"
 #include "om_semiring.cuh"
@@ -108,18 +109,28 @@ __global__ void __launch_bounds__(256) gemm_tiled(GemmArgs g) {
 }
 
 template <typename T, int ALG, bool ARGMAX>
-__global__ void __launch_bounds__(256) gemm_small(GemmArgs g, int64_t total) {
+__global__ void __launch_bounds__(256) gemm_small(GemmArgs g, int64_t total, FastDiv dm,
+                                                  FastDiv dn) {
   using S = Semi<ALG, T>;
   if (g.fast_gate && !fast_path_ruled_out(*g.fast_gate, ALG)) return;
   const T* __restrict__ A = (const T*)g.A;
   const T* __restrict__ B = (const T*)g.B;
   T* __restrict__ C = (T*)g.C;
+  const bool idx32 = total < (int64_t(1) << 32);
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
-    int64_t m = e % g.M;
-    int64_t r = e / g.M;
-    int64_t n = r % g.N;
-    int64_t bt = r / g.N;
+    int64_t m, n, bt;
+    if (idx32) {  // multiply-high divisions instead of 64-bit ones
+      const uint32_t e32 = (uint32_t)e, r = fast_div(e32, dm), q = fast_div(r, dn);
+      m = e32 - r * dm.d;
+      n = r - q * dn.d;
+      bt = q;
+    } else {
+      m = e % g.M;
+      const int64_t r = e / g.M;
+      n = r % g.N;
+      bt = r / g.N;
+    }
     const T* a = A + m * g.sam + bt * g.sab;
     const T* b = B + n * g.sbn + bt * g.sbb;
     T acc = S::zero();
@@ -142,109 +153,200 @@ __global__ void __launch_bounds__(256) gemm_small(GemmArgs g, int64_t total) {
   }
 }
 
-// One thread per output element; every group index is decoded into the
-// operands' offsets mode by mode, so operands whose groups do not flatten are
-// read in place (no gather).  The contracted offsets of A and B are tabulated
-// per block in shared memory when K is small.
-constexpr int kKTable = 1024;
+// gemm_node: one thread per output element of a node read in place through
+// per-mode strides.  Contracted offsets (K <= kNodeKTable) and the offsets of
+// the tile's low output modes are tabulated in shared memory once per block;
+// each tile row decodes its high modes once with 32-bit multiply-high
+// divisions, and every thread then takes P / 256 outputs of the row, so the
+// per-output index work is a few shared-memory reads.  The output is written
+// at its linear index (contiguous, coalesced).
+constexpr int kNodeKTable = 512, kNodeLow = 1024;
 
-__device__ __forceinline__ void decode2(const ModeGroup& g, int64_t i, int64_t& o0, int64_t& o1) {
-  for (int j = 0; j < g.n; ++j) {
-    const int64_t d = i % g.ext[j];
-    i /= g.ext[j];
-    o0 += d * g.s0[j];
-    o1 += d * g.s1[j];
-  }
-}
-
-template <typename T, int ALG, bool ARGMAX>
-__global__ void __launch_bounds__(256) gemm_small_strided(StridedGemmArgs g, int64_t total) {
+template <typename T, int ALG, bool ARGMAX, int KT>
+__global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
   using S = Semi<ALG, T>;
-  __shared__ int64_t ka[kKTable], kb[kKTable];
-  const bool table = g.K <= kKTable;
-  if (table) {
-    for (int64_t k = threadIdx.x; k < g.K; k += blockDim.x) {
+  __shared__ int64_t ka[kNodeKTable], kb[kNodeKTable];
+  __shared__ int64_t la[kNodeLow], lb[kNodeLow];
+  const int tid = threadIdx.x;
+  const bool ktab = g.K <= kNodeKTable;
+  if (ktab)
+    for (int k = tid; k < (int)g.K; k += blockDim.x) {
+      uint32_t r = (uint32_t)k;
       int64_t oa = 0, ob = 0;
-      decode2(g.gk, k, oa, ob);
+      for (int j = 0; j < g.nk; ++j) {
+        const uint32_t q = fast_div(r, g.kmodes[j].div);
+        const uint32_t d = r - q * g.kmodes[j].div.d;
+        oa += (int64_t)d * g.kmodes[j].sa;
+        ob += (int64_t)d * g.kmodes[j].sb;
+        r = q;
+      }
       ka[k] = oa;
       kb[k] = ob;
     }
-    __syncthreads();
+  for (int lo = tid; lo < g.P; lo += blockDim.x) {
+    uint32_t r = (uint32_t)lo;
+    int64_t oa = 0, ob = 0;
+    for (int j = 0; j < g.nlow; ++j) {
+      const uint32_t q = fast_div(r, g.out[j].div);
+      const uint32_t d = r - q * g.out[j].div.d;
+      oa += (int64_t)d * g.out[j].sa;
+      ob += (int64_t)d * g.out[j].sb;
+      r = q;
+    }
+    la[lo] = oa;
+    lb[lo] = ob;
   }
+  __syncthreads();
   const T* __restrict__ A = (const T*)g.A;
   const T* __restrict__ B = (const T*)g.B;
   T* __restrict__ C = (T*)g.C;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = e % g.M, r = e / g.M, n = r % g.N, bt = r / g.N;
-    int64_t oa = 0, ob = 0, oc = 0, t0 = 0;
-    decode2(g.gm, m, oa, oc);
-    decode2(g.gn, n, ob, oc);
-    {
-      int64_t i = bt;
-      for (int j = 0; j < g.gb.n; ++j) {
-        const int64_t d = i % g.gb.ext[j];
-        i /= g.gb.ext[j];
-        oa += d * g.gb.s0[j];
-        ob += d * g.gb.s1[j];
-        oc += d * g.gb.s2[j];
-      }
+  // rows per block iteration: one when the row fills the block, else several
+  const int rpi = g.P >= 256 ? 1 : 256 / g.P;
+  const int sub = g.P >= 256 ? 0 : tid / g.P;
+  const int lo0 = g.P >= 256 ? tid : tid % g.P;
+  const int lstep = g.P >= 256 ? 256 : g.P;
+  if (sub >= rpi) return;
+  for (int64_t r0 = (int64_t)blockIdx.x * rpi; r0 < g.rows; r0 += (int64_t)gridDim.x * rpi) {
+    const int64_t row = r0 + sub;
+    if (row >= g.rows) break;
+    uint32_t r = (uint32_t)row;
+    int64_t ha = 0, hb = 0;
+    for (int j = g.nlow; j < g.nout; ++j) {
+      const uint32_t q = fast_div(r, g.out[j].div);
+      const uint32_t d = r - q * g.out[j].div.d;
+      ha += (int64_t)d * g.out[j].sa;
+      hb += (int64_t)d * g.out[j].sb;
+      r = q;
     }
-    T acc = S::zero();
-    uint32_t idx = 0;
-    for (int64_t k = 0; k < g.K; ++k) {
-      int64_t xa, xb;
-      if (table) {
-        xa = ka[k];
-        xb = kb[k];
-      } else {
-        xa = 0;
-        xb = 0;
-        decode2(g.gk, k, xa, xb);
+    if constexpr (KT > 0) {
+      // K == KT: all loads of the thread's (up to) 4 outputs of this row are
+      // issued before any is used
+      constexpr int U = kNodeLow / 256;
+      int64_t xa[KT], xb[KT];
+#pragma unroll
+      for (int k = 0; k < KT; ++k) {
+        xa[k] = ka[k];
+        xb[k] = kb[k];
       }
-      const T av = A[oa + xa], bv = B[ob + xb];
-      if (ALG == OM_STANDARD) {
-        acc = fma(av, bv, acc);
-      } else {
-        const T p = S::mul(av, bv);
-        if (!S::keep(acc, p)) {
-          acc = p;
-          idx = (uint32_t)k;
+      T av[U][KT], bv[U][KT];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int lo = lo0 + u * lstep;
+        if (lo < g.P) {
+          const T* a = A + ha + la[lo];
+          const T* b = B + hb + lb[lo];
+#pragma unroll
+          for (int k = 0; k < KT; ++k) {
+            av[u][k] = a[xa[k]];
+            bv[u][k] = b[xb[k]];
+          }
         }
       }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int lo = lo0 + u * lstep;
+        if (lo < g.P) {
+          T acc = S::zero();
+          uint32_t idx = 0;
+#pragma unroll
+          for (int k = 0; k < KT; ++k) {
+            if (ALG == OM_STANDARD) {
+              acc = fma(av[u][k], bv[u][k], acc);
+            } else {
+              const T p = S::mul(av[u][k], bv[u][k]);
+              if (!S::keep(acc, p)) {
+                acc = p;
+                idx = (uint32_t)k;
+              }
+            }
+          }
+          const int64_t e = row * g.P + lo;
+          C[e] = acc;
+          if (ARGMAX) g.argmax[e] = (ALG == OM_STANDARD) ? 0u : idx;
+        }
+      }
+    } else {
+    for (int lo = lo0; lo < g.P; lo += lstep) {
+      const T* a = A + ha + la[lo];
+      const T* b = B + hb + lb[lo];
+      T acc = S::zero();
+      uint32_t idx = 0;
+      for (int64_t k = 0; k < g.K; ++k) {
+        int64_t xa, xb;
+        if (ktab) {
+          xa = ka[k];
+          xb = kb[k];
+        } else {
+          xa = xb = 0;
+          uint32_t rk = (uint32_t)k;
+          for (int j = 0; j < g.nk; ++j) {
+            const uint32_t q = fast_div(rk, g.kmodes[j].div);
+            const uint32_t d = rk - q * g.kmodes[j].div.d;
+            xa += (int64_t)d * g.kmodes[j].sa;
+            xb += (int64_t)d * g.kmodes[j].sb;
+            rk = q;
+          }
+        }
+        const T av = a[xa], bv = b[xb];
+        if (ALG == OM_STANDARD) {
+          acc = fma(av, bv, acc);
+        } else {
+          const T p = S::mul(av, bv);
+          if (!S::keep(acc, p)) {
+            acc = p;
+            idx = (uint32_t)k;
+          }
+        }
+      }
+      const int64_t e = row * g.P + lo;
+      C[e] = acc;
+      if (ARGMAX) g.argmax[e] = (ALG == OM_STANDARD) ? 0u : idx;
     }
-    (void)t0;
-    C[oc] = acc;
-    if (ARGMAX) g.argmax[oc] = (ALG == OM_STANDARD) ? 0u : idx;
+    }
   }
 }
 
 template <typename T, int ALG>
-int launch_strided_typed(om_backend* be, const StridedGemmArgs& g) {
-  const int64_t total = g.M * g.N * g.batch;
-  int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)be->num_sms * 64);
+int launch_node_typed(om_backend* be, const NodeArgs& g) {
+  const int rpi = g.P >= 256 ? 1 : 256 / g.P;
+  int64_t blocks = std::min<int64_t>((g.rows + rpi - 1) / rpi, (int64_t)be->num_sms * 16);
   if (blocks < 1) blocks = 1;
-  ProfScope prof(be, "gemm_small_strided");
-  if (g.argmax)
-    gemm_small_strided<T, ALG, true><<<(int)blocks, 256, 0, be->stream>>>(g, total);
-  else
-    gemm_small_strided<T, ALG, false><<<(int)blocks, 256, 0, be->stream>>>(g, total);
+  ProfScope prof(be, "gemm_node");
+  auto go = [&](auto am, auto kt) {
+    gemm_node<T, ALG, decltype(am)::value, decltype(kt)::value><<<(int)blocks, 256, 0, be->stream>>>(g);
+  };
+  auto with_k = [&](auto am) {
+    switch (g.K) {
+      case 1: go(am, std::integral_constant<int, 1>{}); break;
+      case 2: go(am, std::integral_constant<int, 2>{}); break;
+      case 4: go(am, std::integral_constant<int, 4>{}); break;
+      default: go(am, std::integral_constant<int, 0>{}); break;
+    }
+  };
+  if (g.argmax) with_k(std::true_type{});
+  else with_k(std::false_type{});
   note_launch();
-  return check_cuda(cudaGetLastError(), "gemm_small_strided launch");
+  return check_cuda(cudaGetLastError(), "gemm_node launch");
 }
 
 template <typename T, int ALG>
 int launch_typed(om_backend* be, const GemmArgs& g) {
   const int64_t outputs = g.M * g.N * g.batch;
-  const bool small = (g.M * g.N <= 1024) || g.M < 16 || g.N < 16;
+  // thread per output: tiny tiles, and k too short for a tile's reuse to pay
+  const bool small = (g.M * g.N <= 1024) || g.M < 16 || g.N < 16 || g.K <= 8;
   ProfScope prof(be, small ? "gemm_exact_small" : "gemm_exact_tiled");
   if (small) {
     int64_t blocks = std::min<int64_t>((outputs + 255) / 256, (int64_t)be->num_sms * 64);
     if (blocks < 1) blocks = 1;
+    FastDiv dm{}, dn{};
+    if (outputs < (int64_t(1) << 32)) {
+      dm = make_fastdiv((uint32_t)g.M);
+      dn = make_fastdiv((uint32_t)g.N);
+    }
     if (g.argmax)
-      gemm_small<T, ALG, true><<<(int)blocks, 256, 0, be->stream>>>(g, outputs);
+      gemm_small<T, ALG, true><<<(int)blocks, 256, 0, be->stream>>>(g, outputs, dm, dn);
     else
-      gemm_small<T, ALG, false><<<(int)blocks, 256, 0, be->stream>>>(g, outputs);
+      gemm_small<T, ALG, false><<<(int)blocks, 256, 0, be->stream>>>(g, outputs, dm, dn);
   } else {
     dim3 grid((unsigned)((g.M + BM - 1) / BM), (unsigned)((g.N + BN - 1) / BN),
               (unsigned)std::min<int64_t>(g.batch, 65535));
@@ -269,12 +371,15 @@ int launch_gemm_exact(om_backend* be, const GemmArgs& g) {
   return set_error(OM_ERR_UNSUPPORTED, "gemm: dtype must be f32 or f64");
 }
 
-int launch_gemm_small_strided(om_backend* be, const StridedGemmArgs& g) {
-  if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return OM_OK;
+int launch_gemm_node(om_backend* be, const NodeArgs& g) {
+  if (g.total <= 0) return OM_OK;
+  if (g.P < 1 || g.P > kNodeLow || g.rows >= (int64_t(1) << 32) || g.K >= (int64_t(1) << 32) ||
+      g.nout > kMaxNodeModes || g.nk > kMaxNodeModes)
+    return set_error(OM_ERR_INVALID, "gemm_node: plan out of range");
   if (g.dtype == OM_F32) {
-    OM_DISPATCH_ALG(g.alg, ALG, return launch_strided_typed<float, ALG>(be, g));
+    OM_DISPATCH_ALG(g.alg, ALG, return launch_node_typed<float, ALG>(be, g));
   } else if (g.dtype == OM_F64) {
-    OM_DISPATCH_ALG(g.alg, ALG, return launch_strided_typed<double, ALG>(be, g));
+    OM_DISPATCH_ALG(g.alg, ALG, return launch_node_typed<double, ALG>(be, g));
   }
   return set_error(OM_ERR_UNSUPPORTED, "gemm: dtype must be f32 or f64");
 }

@@ -35,6 +35,8 @@ namespace om {
 int set_error(int code, const std::string& msg);
 int check_cuda(cudaError_t e, const char* what);
 void note_launch(int n = 1);
+// OM_B200_TRACE=1 in the environment: one stderr line per planner decision
+bool trace_on();
 
 // Brackets the kernel launches of its lifetime with CUDA events when the
 // backend's profiling is on.
@@ -93,28 +95,56 @@ struct GemmArgs {
 };
 int launch_gemm(om_backend* be, const GemmArgs& g);
 
-// A mode group decoded element by element: index i of the group is the
-// column-major number over its modes (extents ext), and contributes
-// sum_j digit_j * s<op>[j] to each operand's offset.
-constexpr int kMaxGroupModes = 16;
-struct ModeGroup {
-  int n = 0;
-  int64_t ext[kMaxGroupModes];
-  int64_t s0[kMaxGroupModes], s1[kMaxGroupModes], s2[kMaxGroupModes];
+// Unsigned 32-bit division by an invariant divisor d >= 1 with one
+// multiply-high, exact for every dividend below 2^32 (Granlund & Montgomery,
+// "Division by invariant integers using multiplication", PLDI 1994, fig. 4.1):
+// l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1,
+// q = (t + ((n - t) >> min(l, 1))) >> max(l - 1, 0) with t = umulhi(m, n).
+struct FastDiv {
+  uint32_t d, m, s1, s2;
 };
-// Batched small GEMM over strided operands whose groups need not flatten:
-// gm strides (A, C), gn (B, C), gk (A, B), gb (A, B, C).
-struct StridedGemmArgs {
+inline FastDiv make_fastdiv(uint32_t d) {
+  int l = 0;
+  while ((uint64_t(1) << l) < d) ++l;
+  const uint64_t m = ((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1;
+  return FastDiv{d, (uint32_t)m, (uint32_t)(l < 1 ? l : 1), (uint32_t)(l > 0 ? l - 1 : 0)};
+}
+#ifdef __CUDACC__
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv& f) {
+  const uint32_t t = __umulhi(f.m, n);
+  return (t + ((n - t) >> f.s1)) >> f.s2;
+}
+#endif
+
+// Contraction of a small or heavily batched tensor-network node read in
+// place through per-mode strides (no gather, no flattening needed).  The
+// output is contiguous; its modes are listed in memory order with the
+// strides they have in A and B (0 where absent), adjacent modes that are
+// contiguous in both operands merged.  The first nlow output modes (product
+// P) form a tile whose A/B offsets are tabulated per block; the remaining
+// modes are decoded once per tile row.  The contracted modes are listed in
+// modes_a order, so k is the reference's column-major argmax index.
+constexpr int kMaxNodeModes = 40;
+struct NodeMode {
+  FastDiv div;
+  int64_t sa, sb;
+};
+struct NodeArgs {
   om_algebra alg;
   om_dtype dtype;
-  int64_t M, N, K, batch;
+  int64_t K;
+  int64_t total;  // output elements
+  int64_t rows;   // total / P, below 2^32
+  int32_t P;
+  int nlow, nout, nk;
   const void* A;
   const void* B;
   void* C;
   uint32_t* argmax;
-  ModeGroup gm, gn, gk, gb;
+  NodeMode out[kMaxNodeModes];
+  NodeMode kmodes[kMaxNodeModes];
 };
-int launch_gemm_small_strided(om_backend* be, const StridedGemmArgs& g);
+int launch_gemm_node(om_backend* be, const NodeArgs& g);
 
 // Unary einsum (trace / diagonal / reduce / permute / embed).
 int launch_unary(om_backend* be, om_algebra alg, om_dtype dt, const void* x, int nx,

@@ -291,3 +291,70 @@ def test_standard_f32_tensor_core_padded_views(be):
     b = orc.normal(94, ldb * n)
     check_case(be, "standard", a, [m, k], [1, lda], [0, 1], b, [k, n], [1, ldb], [1, 2], [n, m],
                [2, 0], argmax=False)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("shape", [[2] * 14, [2] * 21, [3, 2, 5, 2, 2, 7, 2, 3, 2], [4, 2] * 6,
+                                   [2, 2, 64, 2, 2, 2, 3]])
+def test_copy_strided_dense_permutations(be, shape, dtype):
+    """Permutations of dense tensors with short axes (the tiled permutation
+    path of the gather: network intermediates of extent-2 modes), bit-exact
+    against the oracle's restated copy_strided."""
+    rng = np.random.default_rng(len(shape) * 7 + sum(shape))
+    n = int(np.prod(shape))
+    src = orc.normal(91 + len(shape), n).astype(dtype)
+    s = be.from_slice(src)
+    st = col(shape)
+    for trial in range(4):
+        perm = rng.permutation(len(shape)) if trial else np.arange(len(shape))[::-1]
+        sh = [shape[i] for i in perm]
+        sd = [st[i] for i in perm]
+        got = be.copy_strided(s, sh, sd, 0).to_vec()
+        want = orc.copy_strided(src, sh, sd, 0)
+        assert np.array_equal(got.view(np.uint8), np.asarray(want, dtype).view(np.uint8)), (sh, sd)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul", "standard"])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_node_many_modes_permuted(be, alg, dtype, seed):
+    """Tensor-network nodes with 10-22 extent-2 modes in scrambled orders
+    (batch, free, contracted and trace modes mixed, more than 16 modes in a
+    group): the in-place node kernel against the oracle, values and argmax."""
+    rng = np.random.default_rng(100 + seed)
+    nl = [10, 14, 18][seed]
+    labels = list(range(nl))
+    role = rng.integers(0, 5, nl)  # 0 batch, 1 left, 2 right, 3 contracted, 4 left trace
+    ma = [l for l in labels if role[l] in (0, 1, 3, 4)]
+    mb = [l for l in labels if role[l] in (0, 2, 3)]
+    mc = [l for l in labels if role[l] in (0, 1, 2)]
+    ma = list(rng.permutation(ma))
+    mb = list(rng.permutation(mb))
+    mc = list(rng.permutation(mc))
+    sa, sb, sc = [2] * len(ma), [2] * len(mb), [2] * len(mc)
+    a = orc.ties(300 + seed, 2 ** len(ma), -3, 3).astype(dtype)
+    b = orc.ties(400 + seed, 2 ** len(mb), -3, 3).astype(dtype)
+    if alg == "maxmul":
+        a, b = np.abs(a), np.abs(b)
+    check_case(be, alg, a, sa, col(sa), [int(x) for x in ma], b, sb, col(sb),
+               [int(x) for x in mb], sc, [int(x) for x in mc], argmax=alg != "standard")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("alg", ["maxplus", "standard"])
+def test_node_batched_tiny_k(be, alg):
+    """K = 2 with large, non-flattenable M and N (the thread-per-output path
+    for short contractions) and a long leading output mode."""
+    ma, mb, mc = [0, 1, 2, 3], [2, 4, 3, 5], [5, 0, 4, 3, 1]
+    sa, sb = [96, 3, 2, 40], [2, 64, 40, 3]
+    sc = [3, 96, 64, 40, 3]
+    a = orc.ties(501, int(np.prod(sa)), -4, 4)
+    b = orc.ties(502, int(np.prod(sb)), -4, 4)
+    check_case(be, alg, a, sa, col(sa), ma, b, sb, col(sb), mb, sc, mc, argmax=alg != "standard")
+    # a long contiguous leading output mode (split into tile pieces)
+    ma, mb, mc = [0, 1], [1, 2], [0, 2]
+    check_case(be, alg, orc.ties(503, 4096 * 2, -4, 4), [4096, 2], [2, 1], ma,
+               orc.ties(504, 2 * 3, -4, 4), [2, 3], [1, 2], mb, [4096, 3], mc,
+               argmax=alg != "standard")
