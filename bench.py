@@ -201,7 +201,8 @@ def run_permuted(be, om, local_rank):
     return out
 
 
-NET_N, NET_SLICED = 190, 3
+NET_N = 190
+NET_SLICED = int(os.environ.get("OM_BENCH_NET_SLICED", "3"))
 
 
 def run_network(be, om, world, rank, local_rank, args):

@@ -88,7 +88,14 @@ def order_key(value: float, minimize: bool) -> int:
 
 
 class DeviceExecutor:
-    """Runs one slice on this rank's GPU through om_b200_einsum."""
+    """Runs one slice on this rank's GPU through om_b200_einsum.
+
+    Subtrees none of whose leaves carries a sliced label give the same
+    intermediate in every slice; value() contracts each such maximal subtree
+    once, keeps the result on the device and feeds it to every slice as a
+    leaf of a reduced tree, so a slice only runs the nodes that depend on
+    the sliced labels.  value_and_grad() runs the full tree (its gradient
+    flows to the original leaves)."""
 
     def __init__(self, be, E, alg, ixs, iy, sizes, tensors, tree):
         self.be, self.E, self.alg = be, E, alg
@@ -96,6 +103,7 @@ class DeviceExecutor:
         self.dev = [be.from_slice(t) for t in tensors]
         self.dtype = tensors[0].dtype
         self.enc = E.encode_tree(tree, ixs, iy) if not isinstance(tree, int) else ([], [])
+        self._reduced = {}
 
     def _einsum(self, assign):
         views = sliced_views(self.ixs, self.sizes, assign)
@@ -105,10 +113,69 @@ class DeviceExecutor:
         ein = self.E.Einsum([v[3] for v in views], self.iy, sizes).set_encoded(children, node_iys)
         return ein, views
 
+    def _reduce(self, sliced):
+        """(leaves, encoded reduced tree) for this set of sliced labels;
+        leaves are ('leaf', i) or ('hoisted', Storage, labels)."""
+        key = frozenset(sliced)
+        if key in self._reduced:
+            return self._reduced[key]
+        E = self.E
+        labels = E.tree_output_labels(self.tree, self.ixs, self.iy) \
+            if not isinstance(self.tree, int) else {}
+        leaves, ixs = [], []
+
+        def leafset(t):
+            return [t] if isinstance(t, int) else leafset(t[0]) + leafset(t[1])
+
+        def invariant(t):
+            return all(not (set(self.ixs[i]) & key) for i in leafset(t))
+
+        def rec(t, root=False):
+            if isinstance(t, int):
+                leaves.append(("leaf", t))
+                ixs.append(list(self.ixs[t]))
+                return len(leaves) - 1
+            if not root and invariant(t):
+                sub = leafset(t)
+                pos = {i: j for j, i in enumerate(sub)}
+
+                def remap(u):
+                    return pos[u] if isinstance(u, int) else (remap(u[0]), remap(u[1]))
+                out_l = list(labels[id(t)])
+                ein = E.Einsum([self.ixs[i] for i in sub], out_l, self.sizes)
+                ein.set_contraction_tree(remap(t))
+                val = ein.execute(self.be, self.alg, [self.dev[i] for i in sub])
+                leaves.append(("hoisted", val, out_l))
+                ixs.append(out_l)
+                return len(leaves) - 1
+            return (rec(t[0]), rec(t[1]))
+
+        tree = rec(self.tree, root=True)
+        enc = E.encode_tree(tree, ixs, self.iy) if not isinstance(tree, int) else ([], [])
+        self._reduced[key] = (leaves, ixs, enc)
+        return self._reduced[key]
+
     def value(self, assign):
-        ein, views = self._einsum(assign)
+        leaves, ixs, (children, node_iys) = self._reduce(assign.keys())
+        full = sliced_views(self.ixs, self.sizes, assign)
+        views, tensors = [], []
+        for lf in leaves:
+            if lf[0] == "leaf":
+                views.append(full[lf[1]])
+                tensors.append(self.dev[lf[1]])
+            else:
+                shape = [self.sizes[l] for l in lf[2]]
+                st, s = [], 1
+                for d in shape:
+                    st.append(s)
+                    s *= d
+                views.append((0, shape, st, lf[2]))
+                tensors.append(lf[1])
+        sizes = {l: v for l, v in self.sizes.items() if l not in assign}
+        node_iys = [[l for l in x if l not in assign] for x in node_iys]
+        ein = self.E.Einsum([v[3] for v in views], self.iy, sizes).set_encoded(children, node_iys)
         out = self.be.alloc(ein.out_size(), self.dtype)
-        ein.call_views(self.be, self.alg, self.dev, views, out, None)
+        ein.call_views(self.be, self.alg, tensors, views, out, None)
         return float(out.to_vec()[0])
 
     def value_and_grad(self, assign, dy=1.0):
