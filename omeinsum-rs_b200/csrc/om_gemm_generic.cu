@@ -153,20 +153,39 @@ __global__ void __launch_bounds__(256) gemm_small(GemmArgs g, int64_t total, Fas
   }
 }
 
-// gemm_node: one thread per output element of a node read in place through
-// per-mode strides.  Contracted offsets (K <= kNodeKTable) and the offsets of
-// the tile's low output modes are tabulated in shared memory once per block;
-// each tile row decodes its high modes once with 32-bit multiply-high
-// divisions, and every thread then takes P / 256 outputs of the row, so the
-// per-output index work is a few shared-memory reads.  The output is written
-// at its linear index (contiguous, coalesced).
-constexpr int kNodeKTable = 512, kNodeLow = 1024;
+// gemm_node: a node read in place through per-mode strides.  Contracted
+// offsets (K <= kNodeKTable) and the offsets of the tile's low output modes
+// are tabulated in shared memory once per block; each tile row decodes its
+// high modes once with 32-bit multiply-high divisions.  A thread takes V
+// consecutive outputs at a time (V = 4 when the first output mode allows it:
+// their operand offsets step by that mode's strides and the outputs leave as
+// one 16-byte store), so the per-output index work is a few integer adds.
+// The output is written at its linear index (contiguous, coalesced).
+constexpr int kNodeKTable = 512, kNodeQuads = 1024;
 
-template <typename T, int ALG, bool ARGMAX, int KT>
+template <int V, typename T>
+__device__ __forceinline__ void store_v(T* p, const T (&v)[V]) {
+  if constexpr (V == 4 && sizeof(T) == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  } else if constexpr (V == 4 && sizeof(T) == 8) {
+    reinterpret_cast<double2*>(p)[0] = make_double2(v[0], v[1]);
+    reinterpret_cast<double2*>(p)[1] = make_double2(v[2], v[3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) p[i] = v[i];
+  }
+}
+
+__device__ __forceinline__ void store_idx(uint32_t* p, const uint32_t (&v)[4]) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void store_idx(uint32_t* p, const uint32_t (&v)[1]) { p[0] = v[0]; }
+
+template <typename T, int ALG, bool ARGMAX, int KT, int V>
 __global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
   using S = Semi<ALG, T>;
   __shared__ int64_t ka[kNodeKTable], kb[kNodeKTable];
-  __shared__ int64_t la[kNodeLow], lb[kNodeLow];
+  __shared__ int64_t la[kNodeQuads], lb[kNodeQuads];
   const int tid = threadIdx.x;
   const bool ktab = g.K <= kNodeKTable;
   if (ktab)
@@ -183,8 +202,9 @@ __global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
       ka[k] = oa;
       kb[k] = ob;
     }
-  for (int lo = tid; lo < g.P; lo += blockDim.x) {
-    uint32_t r = (uint32_t)lo;
+  const int Q = g.P / V;  // groups of V outputs in a tile row
+  for (int q0 = tid; q0 < Q; q0 += blockDim.x) {
+    uint32_t r = (uint32_t)(q0 * V);
     int64_t oa = 0, ob = 0;
     for (int j = 0; j < g.nlow; ++j) {
       const uint32_t q = fast_div(r, g.out[j].div);
@@ -193,18 +213,18 @@ __global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
       ob += (int64_t)d * g.out[j].sb;
       r = q;
     }
-    la[lo] = oa;
-    lb[lo] = ob;
+    la[q0] = oa;
+    lb[q0] = ob;
   }
   __syncthreads();
   const T* __restrict__ A = (const T*)g.A;
   const T* __restrict__ B = (const T*)g.B;
   T* __restrict__ C = (T*)g.C;
   // rows per block iteration: one when the row fills the block, else several
-  const int rpi = g.P >= 256 ? 1 : 256 / g.P;
-  const int sub = g.P >= 256 ? 0 : tid / g.P;
-  const int lo0 = g.P >= 256 ? tid : tid % g.P;
-  const int lstep = g.P >= 256 ? 256 : g.P;
+  const int rpi = Q >= 256 ? 1 : 256 / Q;
+  const int sub = Q >= 256 ? 0 : tid / Q;
+  const int q_first = Q >= 256 ? tid : tid % Q;
+  const int q_step = Q >= 256 ? 256 : Q;
   if (sub >= rpi) return;
   for (int64_t r0 = (int64_t)blockIdx.x * rpi; r0 < g.rows; r0 += (int64_t)gridDim.x * rpi) {
     const int64_t row = r0 + sub;
@@ -218,109 +238,109 @@ __global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
       hb += (int64_t)d * g.out[j].sb;
       r = q;
     }
-    if constexpr (KT > 0) {
-      // K == KT: all loads of the thread's (up to) 4 outputs of this row are
-      // issued before any is used
-      constexpr int U = kNodeLow / 256;
-      int64_t xa[KT], xb[KT];
+    for (int q = q_first; q < Q; q += q_step) {
+      const T* a = A + ha + la[q];
+      const T* b = B + hb + lb[q];
+      T acc[V];
+      uint32_t idx[V];
 #pragma unroll
-      for (int k = 0; k < KT; ++k) {
-        xa[k] = ka[k];
-        xb[k] = kb[k];
+      for (int i = 0; i < V; ++i) {
+        acc[i] = S::zero();
+        idx[i] = 0;
       }
-      T av[U][KT], bv[U][KT];
+      if constexpr (KT > 0) {
+        // K == KT: every load of the V outputs is issued before any is used
+        T av[KT][V], bv[KT][V];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int lo = lo0 + u * lstep;
-        if (lo < g.P) {
-          const T* a = A + ha + la[lo];
-          const T* b = B + hb + lb[lo];
+        for (int k = 0; k < KT; ++k) {
+          const T* ak = a + ka[k];
+          const T* bk = b + kb[k];
 #pragma unroll
-          for (int k = 0; k < KT; ++k) {
-            av[u][k] = a[xa[k]];
-            bv[u][k] = b[xb[k]];
+          for (int i = 0; i < V; ++i) {
+            av[k][i] = ak[g.ia[i]];
+            bv[k][i] = bk[g.ib[i]];
           }
         }
-      }
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int lo = lo0 + u * lstep;
-        if (lo < g.P) {
-          T acc = S::zero();
-          uint32_t idx = 0;
+        for (int k = 0; k < KT; ++k)
 #pragma unroll
-          for (int k = 0; k < KT; ++k) {
+          for (int i = 0; i < V; ++i) {
             if (ALG == OM_STANDARD) {
-              acc = fma(av[u][k], bv[u][k], acc);
+              acc[i] = fma(av[k][i], bv[k][i], acc[i]);
             } else {
-              const T p = S::mul(av[u][k], bv[u][k]);
-              if (!S::keep(acc, p)) {
-                acc = p;
-                idx = (uint32_t)k;
+              const T p = S::mul(av[k][i], bv[k][i]);
+              if (!S::keep(acc[i], p)) {
+                acc[i] = p;
+                idx[i] = (uint32_t)k;
               }
             }
           }
-          const int64_t e = row * g.P + lo;
-          C[e] = acc;
-          if (ARGMAX) g.argmax[e] = (ALG == OM_STANDARD) ? 0u : idx;
-        }
-      }
-    } else {
-    for (int lo = lo0; lo < g.P; lo += lstep) {
-      const T* a = A + ha + la[lo];
-      const T* b = B + hb + lb[lo];
-      T acc = S::zero();
-      uint32_t idx = 0;
-      for (int64_t k = 0; k < g.K; ++k) {
-        int64_t xa, xb;
-        if (ktab) {
-          xa = ka[k];
-          xb = kb[k];
-        } else {
-          xa = xb = 0;
-          uint32_t rk = (uint32_t)k;
-          for (int j = 0; j < g.nk; ++j) {
-            const uint32_t q = fast_div(rk, g.kmodes[j].div);
-            const uint32_t d = rk - q * g.kmodes[j].div.d;
-            xa += (int64_t)d * g.kmodes[j].sa;
-            xb += (int64_t)d * g.kmodes[j].sb;
-            rk = q;
+      } else {
+        for (int64_t k = 0; k < g.K; ++k) {
+          int64_t xa, xb;
+          if (ktab) {
+            xa = ka[k];
+            xb = kb[k];
+          } else {
+            xa = xb = 0;
+            uint32_t rk = (uint32_t)k;
+            for (int j = 0; j < g.nk; ++j) {
+              const uint32_t qq = fast_div(rk, g.kmodes[j].div);
+              const uint32_t d = rk - qq * g.kmodes[j].div.d;
+              xa += (int64_t)d * g.kmodes[j].sa;
+              xb += (int64_t)d * g.kmodes[j].sb;
+              rk = qq;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            const T av = a[xa + g.ia[i]], bv = b[xb + g.ib[i]];
+            if (ALG == OM_STANDARD) {
+              acc[i] = fma(av, bv, acc[i]);
+            } else {
+              const T p = S::mul(av, bv);
+              if (!S::keep(acc[i], p)) {
+                acc[i] = p;
+                idx[i] = (uint32_t)k;
+              }
+            }
           }
         }
-        const T av = a[xa], bv = b[xb];
+      }
+      const int64_t e = row * g.P + (int64_t)q * V;
+      store_v<V>(C + e, acc);
+      if (ARGMAX) {
         if (ALG == OM_STANDARD) {
-          acc = fma(av, bv, acc);
-        } else {
-          const T p = S::mul(av, bv);
-          if (!S::keep(acc, p)) {
-            acc = p;
-            idx = (uint32_t)k;
-          }
+#pragma unroll
+          for (int i = 0; i < V; ++i) idx[i] = 0;
         }
+        store_idx(g.argmax + e, idx);
       }
-      const int64_t e = row * g.P + lo;
-      C[e] = acc;
-      if (ARGMAX) g.argmax[e] = (ALG == OM_STANDARD) ? 0u : idx;
-    }
     }
   }
 }
 
 template <typename T, int ALG>
-int launch_node_typed(om_backend* be, const NodeArgs& g) {
-  const int rpi = g.P >= 256 ? 1 : 256 / g.P;
+int launch_node_typed(om_backend* be, const NodeArgs& g, int vec) {
+  const int Q = g.P / vec;
+  const int rpi = Q >= 256 ? 1 : 256 / Q;
   int64_t blocks = std::min<int64_t>((g.rows + rpi - 1) / rpi, (int64_t)be->num_sms * 16);
   if (blocks < 1) blocks = 1;
   ProfScope prof(be, "gemm_node");
-  auto go = [&](auto am, auto kt) {
-    gemm_node<T, ALG, decltype(am)::value, decltype(kt)::value><<<(int)blocks, 256, 0, be->stream>>>(g);
+  auto go = [&](auto am, auto kt, auto v) {
+    gemm_node<T, ALG, decltype(am)::value, decltype(kt)::value, decltype(v)::value>
+        <<<(int)blocks, 256, 0, be->stream>>>(g);
+  };
+  auto with_v = [&](auto am, auto kt) {
+    if (vec == 4) go(am, kt, std::integral_constant<int, 4>{});
+    else go(am, kt, std::integral_constant<int, 1>{});
   };
   auto with_k = [&](auto am) {
     switch (g.K) {
-      case 1: go(am, std::integral_constant<int, 1>{}); break;
-      case 2: go(am, std::integral_constant<int, 2>{}); break;
-      case 4: go(am, std::integral_constant<int, 4>{}); break;
-      default: go(am, std::integral_constant<int, 0>{}); break;
+      case 1: with_v(am, std::integral_constant<int, 1>{}); break;
+      case 2: with_v(am, std::integral_constant<int, 2>{}); break;
+      case 4: with_v(am, std::integral_constant<int, 4>{}); break;
+      default: with_v(am, std::integral_constant<int, 0>{}); break;
     }
   };
   if (g.argmax) with_k(std::true_type{});
@@ -371,15 +391,57 @@ int launch_gemm_exact(om_backend* be, const GemmArgs& g) {
   return set_error(OM_ERR_UNSUPPORTED, "gemm: dtype must be f32 or f64");
 }
 
-int launch_gemm_node(om_backend* be, const NodeArgs& g) {
-  if (g.total <= 0) return OM_OK;
-  if (g.P < 1 || g.P > kNodeLow || g.rows >= (int64_t(1) << 32) || g.K >= (int64_t(1) << 32) ||
-      g.nout > kMaxNodeModes || g.nk > kMaxNodeModes)
+int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
+  if (g0.total <= 0) return OM_OK;
+  if (g0.K >= (int64_t(1) << 32) || g0.nout > kMaxNodeModes || g0.nk > kMaxNodeModes)
     return set_error(OM_ERR_INVALID, "gemm_node: plan out of range");
+  // V = 4 outputs per thread when the first output mode splits into groups
+  // of four and the outputs take 16-byte stores; the tile row then spans up
+  // to 4 * kNodeQuads outputs
+  NodeArgs g = g0;
+  const size_t es = dtype_size(g.dtype);
+  // a group of 4 consecutive outputs must decode separably: 4 = (product of
+  // the leading modes) x (a divisor of the next mode's extent)
+  bool sep = false;
+  {
+    int64_t pre = 1;
+    for (int j = 0; j < g.nout && !sep; ++j) {
+      const int64_t e = g.out[j].div.d;
+      if (4 % pre == 0 && e % (4 / pre) == 0) sep = true;
+      pre *= e;
+      if (pre > 4) break;
+    }
+  }
+  const bool v4 = sep && g.total % 4 == 0 && ((uintptr_t)g.C % (4 * es)) == 0 &&
+                  (!g.argmax || ((uintptr_t)g.argmax % 16) == 0);
+  int vec = v4 ? 4 : 1;
+  auto tile = [&](int v) {
+    g.nlow = 0;
+    int64_t P = 1;
+    while (g.nlow < g.nout && P * g.out[g.nlow].div.d <= (int64_t)kNodeQuads * v)
+      P *= g.out[g.nlow++].div.d;
+    return P;
+  };
+  int64_t P = tile(vec);
+  if (P % vec) P = tile(vec = 1);
+  for (int i = 0; i < 4; ++i) {
+    g.ia[i] = g.ib[i] = 0;
+    if (i >= vec) continue;
+    int64_t r = i;
+    for (int j = 0; j < g.nout && r; ++j) {
+      const int64_t e = g.out[j].div.d;
+      g.ia[i] += (r % e) * g.out[j].sa;
+      g.ib[i] += (r % e) * g.out[j].sb;
+      r /= e;
+    }
+  }
+  g.P = (int32_t)P;
+  g.rows = g.total / P;
+  if (g.rows >= (int64_t(1) << 32)) return set_error(OM_ERR_INVALID, "gemm_node: too many rows");
   if (g.dtype == OM_F32) {
-    OM_DISPATCH_ALG(g.alg, ALG, return launch_node_typed<float, ALG>(be, g));
+    OM_DISPATCH_ALG(g.alg, ALG, return launch_node_typed<float, ALG>(be, g, vec));
   } else if (g.dtype == OM_F64) {
-    OM_DISPATCH_ALG(g.alg, ALG, return launch_node_typed<double, ALG>(be, g));
+    OM_DISPATCH_ALG(g.alg, ALG, return launch_node_typed<double, ALG>(be, g, vec));
   }
   return set_error(OM_ERR_UNSUPPORTED, "gemm: dtype must be f32 or f64");
 }

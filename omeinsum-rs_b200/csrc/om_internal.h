@@ -143,6 +143,7 @@ struct NodeArgs {
   uint32_t* argmax;
   NodeMode out[kMaxNodeModes];
   NodeMode kmodes[kMaxNodeModes];
+  int64_t ia[4], ib[4];  // A/B offsets of the outputs inside a group of 4 (set by the launcher)
 };
 int launch_gemm_node(om_backend* be, const NodeArgs& g);
 
