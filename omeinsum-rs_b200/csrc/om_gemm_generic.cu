@@ -181,6 +181,46 @@ __device__ __forceinline__ void store_idx(uint32_t* p, const uint32_t (&v)[4]) {
 }
 __device__ __forceinline__ void store_idx(uint32_t* p, const uint32_t (&v)[1]) { p[0] = v[0]; }
 
+// The V values of a group at p + off[i]: one 16-byte load when they are
+// contiguous (w = 4) and aligned, two 8/16-byte loads for two pairs (w = 2),
+// one load when all four coincide (w = 0, a broadcast operand), else scalar
+// loads.  Alignment is tested per group.
+template <int V, typename T>
+__device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], int w,
+                                           T (&out)[V]) {
+  if constexpr (V == 4) {
+    if (w == 0) {
+      out[0] = out[1] = out[2] = out[3] = p[0];
+      return;
+    }
+    if (w == 4 && ((uintptr_t)p & (4 * sizeof(T) - 1)) == 0) {
+      if constexpr (sizeof(T) == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(p);
+        out[0] = v.x, out[1] = v.y, out[2] = v.z, out[3] = v.w;
+      } else {
+        const double2 v0 = reinterpret_cast<const double2*>(p)[0];
+        const double2 v1 = reinterpret_cast<const double2*>(p)[1];
+        out[0] = v0.x, out[1] = v0.y, out[2] = v1.x, out[3] = v1.y;
+      }
+      return;
+    }
+    if (w >= 2 && (((uintptr_t)p | (uintptr_t)(p + off[2])) & (2 * sizeof(T) - 1)) == 0) {
+      if constexpr (sizeof(T) == 4) {
+        const float2 v0 = *reinterpret_cast<const float2*>(p);
+        const float2 v1 = *reinterpret_cast<const float2*>(p + off[2]);
+        out[0] = v0.x, out[1] = v0.y, out[2] = v1.x, out[3] = v1.y;
+      } else {
+        const double2 v0 = *reinterpret_cast<const double2*>(p);
+        const double2 v1 = *reinterpret_cast<const double2*>(p + off[2]);
+        out[0] = v0.x, out[1] = v0.y, out[2] = v1.x, out[3] = v1.y;
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) out[i] = p[off[i]];
+}
+
 template <typename T, int ALG, bool ARGMAX, int KT, int V>
 __global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
   using S = Semi<ALG, T>;
@@ -253,13 +293,8 @@ __global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
         T av[KT][V], bv[KT][V];
 #pragma unroll
         for (int k = 0; k < KT; ++k) {
-          const T* ak = a + ka[k];
-          const T* bk = b + kb[k];
-#pragma unroll
-          for (int i = 0; i < V; ++i) {
-            av[k][i] = ak[g.ia[i]];
-            bv[k][i] = bk[g.ib[i]];
-          }
+          load_group<V>(a + ka[k], g.ia, g.wa, av[k]);
+          load_group<V>(b + kb[k], g.ib, g.wb, bv[k]);
         }
 #pragma unroll
         for (int k = 0; k < KT; ++k)
@@ -324,7 +359,7 @@ template <typename T, int ALG>
 int launch_node_typed(om_backend* be, const NodeArgs& g, int vec) {
   const int Q = g.P / vec;
   const int rpi = Q >= 256 ? 1 : 256 / Q;
-  int64_t blocks = std::min<int64_t>((g.rows + rpi - 1) / rpi, (int64_t)be->num_sms * 16);
+  int64_t blocks = std::min<int64_t>((g.rows + rpi - 1) / rpi, (int64_t)be->num_sms * 8);
   if (blocks < 1) blocks = 1;
   ProfScope prof(be, "gemm_node");
   auto go = [&](auto am, auto kt, auto v) {
@@ -424,6 +459,12 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
   };
   int64_t P = tile(vec);
   if (P % vec) P = tile(vec = 1);
+  auto width = [&](const int64_t* o) {
+    if (vec != 4) return 1;
+    if (o[1] == 0 && o[2] == 0 && o[3] == 0) return 0;
+    if (o[1] == 1 && o[2] == 2 && o[3] == 3) return 4;
+    return (o[1] == 1 && o[3] == o[2] + 1) ? 2 : 1;
+  };
   for (int i = 0; i < 4; ++i) {
     g.ia[i] = g.ib[i] = 0;
     if (i >= vec) continue;
@@ -435,6 +476,8 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
       r /= e;
     }
   }
+  g.wa = width(g.ia);
+  g.wb = width(g.ib);
   g.P = (int32_t)P;
   g.rows = g.total / P;
   if (g.rows >= (int64_t(1) << 32)) return set_error(OM_ERR_INVALID, "gemm_node: too many rows");

@@ -144,6 +144,7 @@ struct NodeArgs {
   NodeMode out[kMaxNodeModes];
   NodeMode kmodes[kMaxNodeModes];
   int64_t ia[4], ib[4];  // A/B offsets of the outputs inside a group of 4 (set by the launcher)
+  int wa, wb;            // 4: ia = {0,1,2,3}; 2: pairs {0,1},{x,x+1}; 0: all 0; 1: other
 };
 int launch_gemm_node(om_backend* be, const NodeArgs& g);
 
