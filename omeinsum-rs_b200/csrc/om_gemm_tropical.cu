@@ -38,6 +38,7 @@ namespace om {
 namespace {
 
 constexpr int TB_M = 128, TB_N = 64, TB_K = 32, NT = 256, NE = 32;
+constexpr int kWin = 64;  // argmax resolve: slabs bucketed per window
 
 __device__ __forceinline__ unsigned long long pk_add(unsigned long long a, unsigned long long b) {
   unsigned long long d;
@@ -329,7 +330,11 @@ __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
   float* Bs0 = As0 + 2 * TB_K * TB_M;  // 2 x TB_K*TB_N floats
   float* vals = (float*)smem + resolve_region<A_MC, B_KC>();  // [NE][NT] (ARGMAX)
   uint32_t* kres = (uint32_t*)vals;  // resolved k of an output overwrites its value
-  uint32_t* stage = (uint32_t*)(vals + NE * NT);              // [8 warps][64] items
+  // resolve bookkeeping (ARGMAX): outputs bucketed by deciding slab
+  uint16_t* items = (uint16_t*)(vals + NE * NT);            // [NE * NT] (thread << 5 | e)
+  int* bcount = (int*)(items + NE * NT);  // [kWin + 2]: counts, then offsets; [kWin + 1]: list size
+  int* bcur = bcount + kWin + 2;                            // [kWin] scatter cursors
+  int* blist = bcur + kWin;                                 // [kWin] non-empty slabs, last first
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r0 = row_of(warp, lane, 0), c0 = col_of(warp, lane, 0);
@@ -421,56 +426,118 @@ __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
       for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) vals[(i * 4 + j) * NT + tid] = acc[i][j];
-      uint32_t* items = stage + warp * 64;
-      // Resolve pass over the piece's slabs, last first: the deciding slab of
-      // an output is the last one whose bit is set.  Items of a slab are
-      // compacted across the warp so every lane scans at most one output per
-      // round; the found k replaces the output's value in shared memory.
+      // Resolve pass.  The deciding slab of an output is the last slab of the
+      // piece whose improvement bit is set.  Windows of kWin slabs are taken
+      // last first; in each, the outputs are bucketed by deciding slab (a
+      // counting sort over the whole CTA), then only the slabs that decide
+      // something are re-staged (cp.async, two stages) and every thread scans
+      // at most one output of the slab per round for the first k whose
+      // product equals the final value.  The found k replaces the output's
+      // value in shared memory.
       using RS = ResolveStager<A_MC, B_KC>;
       RS rs;
       auto stA = [&](int q) { return (float*)smem + q * RS::STAGE; };
       auto stB = [&](int q) { return (float*)smem + q * RS::STAGE + RS::A_FLOATS; };
-      rs.issue(g, Ab, Bb, m0, n0, te - 1, stA(0), stB(0), tid);
-      uint32_t mask_next = masks[(size_t)(te - 1 - tb) * NT + tid];
-      for (int t = te - 1; t >= tb; --t) {
-        const int s = (te - 1 - t) & 1;
-        const float* RA = stA(s);
-        const float* RB = stB(s);
-        const uint32_t mine = mask_next & remaining;
-        if (t > tb) {
-          rs.issue(g, Ab, Bb, m0, n0, t - 1, stA(s ^ 1), stB(s ^ 1), tid);
-          mask_next = masks[(size_t)(t - 1 - tb) * NT + tid];
-          cp_async_wait<1>();
-        } else {
-          cp_async_wait<0>();
+      for (int whi = te; whi > tb; whi -= kWin) {
+        const int wlo = whi - kWin > tb ? whi - kWin : tb;
+        const int wn = whi - wlo;
+        for (int q = tid; q < kWin + 2; q += NT) bcount[q] = 0;
+        __syncthreads();
+        // pass 1: count the outputs each slab of the window decides (mask
+        // words are fetched 16 at a time so their L2 latencies overlap)
+        uint32_t rem = remaining;
+        for (int t1 = whi; t1 > wlo && rem; t1 -= 16) {
+          uint32_t mw[16];
+#pragma unroll
+          for (int x = 0; x < 16; ++x)
+            mw[x] = (t1 - 1 - x >= wlo) ? __ldcg(masks + (size_t)(t1 - 1 - x - tb) * NT + tid) : 0u;
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            const uint32_t m = mw[x] & rem;
+            rem &= ~m;
+            if (m) atomicAdd(bcount + (t1 - 1 - x - wlo), __popc(m));
+          }
         }
         __syncthreads();
-        remaining &= ~mine;
-        const int cnt = __popc(mine);
-        int pos = cnt;  // inclusive warp scan
+        if (warp == 0) {  // exclusive scan of the counts; list of non-empty slabs
+          int carry = 0, nlist = 0;
+          for (int base = 0; base < wn; base += 32) {
+            const int q = base + lane;
+            const int c = q < wn ? bcount[q] : 0;
+            int x = c;
 #pragma unroll
-        for (int d = 1; d < 32; d <<= 1) {
-          const int v = __shfl_up_sync(0xffffffffu, pos, d);
-          if (lane >= d) pos += v;
-        }
-        const int total = __shfl_sync(0xffffffffu, pos, 31);
-        const int kmax = min(TB_K, g.K - t * TB_K);
-        for (int done = 0; done < total; done += 64) {
-          uint32_t rest = mine;
-          int p = pos - cnt;
-          while (rest) {
-            const int e = __ffs(rest) - 1;
-            rest &= rest - 1;
-            if (p >= done && p < done + 64) items[p - done] = ((uint32_t)lane << 5) | (uint32_t)e;
-            ++p;
+            for (int d = 1; d < 32; d <<= 1) {
+              const int y = __shfl_up_sync(0xffffffffu, x, d);
+              if (lane >= d) x += y;
+            }
+            if (q < wn) {
+              bcount[q] = carry + x - c;
+              bcur[q] = carry + x - c;
+            }
+            carry += __shfl_sync(0xffffffffu, x, 31);
+            // non-empty slabs, highest first: slab wlo + q at list position
+            // (number of non-empty slabs above it)
+            const unsigned nz = __ballot_sync(0xffffffffu, c > 0);
+            if (c > 0) blist[nlist + __popc(nz & ((1u << lane) - 1))] = q;
+            nlist += __popc(nz);
           }
+          if (lane == 0) {
+            bcount[wn] = carry;  // end of the last bucket
+            bcount[kWin + 1] = nlist;
+          }
+          // reverse the list in place so that it runs from the last slab down
           __syncwarp();
-          const int here = min(64, total - done);
-          for (int q = lane; q < here; q += 32) {
-            const uint32_t it = items[q];
+          for (int q = lane; q < nlist / 2; q += 32) {
+            const int x = blist[q], y = blist[nlist - 1 - q];
+            blist[q] = y;
+            blist[nlist - 1 - q] = x;
+          }
+        }
+        __syncthreads();
+        // pass 2: scatter the outputs into their slab's bucket
+        rem = remaining;
+        for (int t1 = whi; t1 > wlo && rem; t1 -= 16) {
+          uint32_t mw[16];
+#pragma unroll
+          for (int x = 0; x < 16; ++x)
+            mw[x] = (t1 - 1 - x >= wlo) ? __ldcg(masks + (size_t)(t1 - 1 - x - tb) * NT + tid) : 0u;
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            uint32_t m = mw[x] & rem;
+            rem &= ~m;
+            if (m) {
+              int at = atomicAdd(bcur + (t1 - 1 - x - wlo), __popc(m));
+              while (m) {
+                const int e = __ffs(m) - 1;
+                m &= m - 1;
+                items[at++] = (uint16_t)((tid << 5) | e);
+              }
+            }
+          }
+        }
+        remaining = rem;
+        const int nlist = bcount[kWin + 1];
+        __syncthreads();
+        // re-stage and scan the deciding slabs, last first
+        if (nlist > 0) rs.issue(g, Ab, Bb, m0, n0, wlo + blist[0], stA(0), stB(0), tid);
+        for (int li = 0; li < nlist; ++li) {
+          const int q = blist[li], t = wlo + q, s = li & 1;
+          if (li + 1 < nlist) {
+            rs.issue(g, Ab, Bb, m0, n0, wlo + blist[li + 1], stA(s ^ 1), stB(s ^ 1), tid);
+            cp_async_wait<1>();
+          } else {
+            cp_async_wait<0>();
+          }
+          __syncthreads();
+          const float* RA = stA(s);
+          const float* RB = stB(s);
+          const int b0 = bcount[q], b1 = bcount[q + 1];
+          const int kmax = min(TB_K, g.K - t * TB_K);
+          for (int x = b0 + tid; x < b1; x += NT) {
+            const uint32_t it = items[x];
             const int src = (int)(it >> 5), e = (int)(it & 31);
-            const int mi = row_of(warp, src, e >> 2), nj = col_of(warp, src, e & 3);
-            const int slot = e * NT + warp * 32 + src;
+            const int mi = row_of(src >> 5, src & 31, e >> 2), nj = col_of(src >> 5, src & 31, e & 3);
+            const int slot = e * NT + src;
             const float v = vals[slot];
             int kb = 0;
 #pragma unroll
@@ -480,9 +547,8 @@ __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
             }
             kres[slot] = (uint32_t)(t * TB_K + kb);
           }
-          __syncwarp();
+          __syncthreads();
         }
-        __syncthreads();
       }
     }
 
@@ -576,7 +642,8 @@ __global__ void special_scan_kernel(ScanArgs s0, ScanArgs s1, uint32_t* flags) {
 template <int ALG, bool ARGMAX, bool A_MC, bool B_KC>
 int launch_fast(om_backend* be, const FastArgs& fa, int64_t grid_ctas) {
   const size_t smem =
-      ARGMAX ? sizeof(float) * (resolve_region<A_MC, B_KC>() + NE * NT) + 8 * 64 * sizeof(uint32_t)
+      ARGMAX ? sizeof(float) * (resolve_region<A_MC, B_KC>() + NE * NT) +
+                   sizeof(uint16_t) * NE * NT + sizeof(int) * (3 * kWin + 2)
              : sizeof(float) * 2 * TB_K * (TB_M + TB_N);
   auto kern = tropical_fast_kernel<ALG, ARGMAX, A_MC, B_KC>;
   OM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
