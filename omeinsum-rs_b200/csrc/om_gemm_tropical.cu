@@ -24,10 +24,11 @@
 // output sets a bit when the running max strictly improved inside the slab;
 // the 32-bit mask of a thread is written to a global workspace.  The last
 // slab with the bit set holds the first k reaching the final max, because
-// every earlier slab's max is strictly smaller.  A resolve pass walks the
-// slabs backwards, re-stages each one with cp.async (two stages), and scans
-// only the outputs it decides (compacted across the warp) for the first k
-// with a (x) b == max; ties go to the smallest k and outputs that never beat
+// every earlier slab's max is strictly smaller.  A resolve pass buckets the
+// tile's outputs by deciding slab (a counting sort across the CTA), re-stages
+// only the slabs that decide something with cp.async (two stages), and scans
+// each output once, in its deciding slab, for the first k with
+// a (x) b == max; ties go to the smallest k and outputs that never beat
 // zero() keep argmax 0, as in the reference.
 #include <algorithm>
 
