@@ -242,6 +242,16 @@ def run_network(be, om, world, rank, local_rank, args):
     be.synchronize()
     torch.cuda.synchronize()
     ms = torch.tensor([t0.elapsed_time(t1) / reps], dtype=torch.float64, device=dev)
+    # the two kinds of slice work, timed apart on this rank (diagnostic)
+    assigns = N.slice_assignments(sliced, sizes)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(stream)
+    ex.value(assigns[0])
+    e1.record(stream)
+    ex.value_and_grad(assigns[0])
+    e2.record(stream)
+    be.synchronize()
+    value_ms, grad_ms = e0.elapsed_time(e1), e1.elapsed_time(e2)
     if dist is not None:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     sel = [int(x[1] > x[0]) for x in g[:NET_N]]
@@ -253,6 +263,8 @@ def run_network(be, om, world, rank, local_rank, args):
             "log2_tc": round(float(np.log2(tc)), 2), "log2_sc": round(float(np.log2(sc)), 2),
             "per_slice_log2_tc": round(float(np.log2(tcs)), 2),
             "per_slice_log2_sc": round(float(np.log2(scs)), 2),
+            "slices": 2 ** NET_SLICED, "slice_value_ms": round(value_ms, 3),
+            "slice_value_and_grad_ms": round(grad_ms, 3),
             "order": "min-fill elimination, best of 8 seeded restarts (omeco TreeSA unavailable)",
             "timing": "CUDA events on the backend stream around 3 full runs, max over ranks"}
 

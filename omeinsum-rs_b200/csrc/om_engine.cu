@@ -20,6 +20,7 @@
 // instead (node_order); the root is finalised to iy.  The tape keys every
 // gradient by label, so these orders change no result.
 #include <algorithm>
+#include <cstring>
 #include <map>
 #include <memory>
 #include <string>
@@ -87,6 +88,81 @@ __global__ void scatter_add_kernel(const T* __restrict__ dy, const uint32_t* __r
        o += (int64_t)gridDim.x * blockDim.x)
     if (dy[o] != T(0)) atomicAdd(grad + am[o], dy[o]);  // zeros change no sum
 }
+
+// ---- sparse tropical backward: the whole tape in one launch ---------------
+// A small root gradient (e.g. the scalar of an optimisation problem) is
+// routed down the tape as a list of element indices, one list per node, the
+// values staying those of the root entries (a tropical step only moves them).
+// One block walks the tape level by level from the root: an entry of a
+// binary node is decoded through the node's argmax into one element of each
+// child; an entry of a unary node moves to the element its argmax names; an
+// entry reaching a leaf is added to the leaf's gradient (zeros skipped, as
+// in the dense form).
+struct SpNode {
+  int kind;  // 0 leaf, 1 unary, 2 binary
+  int child0, child1;
+  int nc, nk;   // binary: output and contracted modes
+  int off;      // binary: first record in SpMode data (nc output modes, then nk contracted)
+  const uint32_t* argmax;
+  void* grad;   // leaf
+};
+struct SpMode {
+  int64_t ext, sa, sb;  // extent; element stride in the left / right child (0 if absent)
+};
+
+template <typename T>
+__global__ void __launch_bounds__(512) sparse_backward_kernel(const SpNode* __restrict__ nodes,
+                                                              const SpMode* __restrict__ modes,
+                                                              const int* __restrict__ level_start,
+                                                              int nlevels, int root, int64_t* lists,
+                                                              const T* __restrict__ val, int64_t n) {
+  for (int64_t e = threadIdx.x; e < n; e += blockDim.x) lists[(int64_t)root * n + e] = e;
+  __syncthreads();
+  for (int L = 0; L < nlevels; ++L) {
+    const int first = level_start[L];
+    const int64_t items = (int64_t)(level_start[L + 1] - first) * n;
+    for (int64_t it = threadIdx.x; it < items; it += blockDim.x) {
+      const int id = first + (int)(it / n);
+      const int64_t e = it % n;
+      const SpNode nd = nodes[id];
+      const int64_t o = lists[(int64_t)id * n + e];
+      if (nd.kind == 0) {
+        const T v = val[e];
+        if (v != T(0)) atomicAdd((T*)nd.grad + o, v);
+      } else if (nd.kind == 1) {
+        lists[(int64_t)nd.child0 * n + e] = nd.argmax[o];
+      } else {
+        int64_t pa = 0, pb = 0, rem = o;
+        const SpMode* m = modes + nd.off;
+        for (int k = 0; k < nd.nc; ++k) {
+          const int64_t c = rem % m[k].ext;
+          rem /= m[k].ext;
+          pa += c * m[k].sa;
+          pb += c * m[k].sb;
+        }
+        int64_t w = nd.argmax[o];
+        for (int k = nd.nc; k < nd.nc + nd.nk; ++k) {
+          const int64_t c = w % m[k].ext;
+          w /= m[k].ext;
+          pa += c * m[k].sa;
+          pb += c * m[k].sb;
+        }
+        lists[(int64_t)nd.child0 * n + e] = pa;
+        lists[(int64_t)nd.child1 * n + e] = pb;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+__global__ void zero_many_kernel(T* const* ptrs, const int64_t* sizes, int count) {
+  for (int q = blockIdx.x; q < count; q += gridDim.x)
+    for (int64_t i = threadIdx.x; i < sizes[q]; i += blockDim.x) ptrs[q][i] = T(0);
+}
+
+// Root gradients with at most this many elements take the sparse path.
+constexpr int64_t kSparseGradMax = 4096;
 
 }  // namespace
 
@@ -247,7 +323,133 @@ struct Engine {
   }
 
   int backprop(int idx, const DTensor& dy, void* const* grads);
+  int backprop_sparse(const void* dy, void* const* grads);
 };
+
+// Tropical backward for a small root gradient: the tape is laid out level
+// by level from the root and walked by sparse_backward_kernel in one launch.
+int Engine::backprop_sparse(const void* dy, void* const* grads) {
+  const int64_t n = nodes[root].content.numel();
+  std::vector<int> order{root}, level_start{0}, slot(nodes.size(), -1);
+  slot[root] = 0;
+  for (size_t head = 0; head < order.size();) {
+    const size_t end = order.size();
+    level_start.push_back((int)end);
+    for (; head < end; ++head) {
+      const TapeNode& t = nodes[order[head]];
+      for (int c : {t.child0, t.child1})
+        if (c >= 0 && t.op != Op::Leaf && slot[c] < 0) {
+          slot[c] = (int)order.size();
+          order.push_back(c);
+        }
+    }
+    if (order.size() == end) break;
+  }
+  if (level_start.back() != (int)order.size()) level_start.push_back((int)order.size());
+  // drop a repeated final boundary
+  while (level_start.size() >= 2 && level_start[level_start.size() - 2] == level_start.back())
+    level_start.pop_back();
+  std::vector<SpNode> recs(order.size());
+  std::vector<SpMode> modes;
+  std::vector<void*> zptr;
+  std::vector<int64_t> zsize;
+  for (size_t q = 0; q < order.size(); ++q) {
+    const TapeNode& t = nodes[order[q]];
+    SpNode r{};
+    if (t.op == Op::Leaf) {
+      r.kind = 0;
+      r.grad = grads[t.tensor_index];
+      zptr.push_back(r.grad);
+      zsize.push_back(t.content.numel());
+    } else if (t.op == Op::Unary) {
+      r.kind = 1;
+      r.child0 = slot[t.child0];
+      r.argmax = (const uint32_t*)t.argmax.get();
+    } else {
+      r.kind = 2;
+      r.child0 = slot[t.child0];
+      r.child1 = slot[t.child1];
+      r.argmax = (const uint32_t*)t.argmax.get();
+      r.off = (int)modes.size();
+      const DTensor& l = nodes[t.child0].content;
+      const DTensor& rr = nodes[t.child1].content;
+      auto stride_in = [](const std::vector<int32_t>& ix, const std::vector<int64_t>& shape,
+                          int32_t lab) -> int64_t {
+        int64_t s = 1;
+        for (size_t i = 0; i < ix.size(); ++i) {
+          if (ix[i] == lab) return s;
+          s *= shape[i];
+        }
+        return 0;
+      };
+      const DTensor& c = t.content;
+      for (size_t k = 0; k < t.out_ix.size(); ++k)
+        modes.push_back({c.shape[k], stride_in(t.left_ix, l.shape, t.out_ix[k]),
+                         stride_in(t.right_ix, rr.shape, t.out_ix[k])});
+      r.nc = (int)t.out_ix.size();
+      // contracted labels in left_ix order: the argmax's column-major digits
+      for (size_t k = 0; k < t.left_ix.size(); ++k) {
+        const int32_t lab = t.left_ix[k];
+        const bool in_r = std::find(t.right_ix.begin(), t.right_ix.end(), lab) != t.right_ix.end();
+        const bool in_c = std::find(t.out_ix.begin(), t.out_ix.end(), lab) != t.out_ix.end();
+        if (in_r && !in_c) {
+          modes.push_back({l.shape[k], stride_in(t.left_ix, l.shape, lab),
+                           stride_in(t.right_ix, rr.shape, lab)});
+          r.nk++;
+        }
+      }
+    }
+    recs[q] = r;
+  }
+  int rc;
+  const size_t b_nodes = sizeof(SpNode) * recs.size(), b_modes = sizeof(SpMode) * modes.size();
+  const size_t b_levels = sizeof(int) * level_start.size(), b_lists = 8 * order.size() * (size_t)n;
+  const size_t b_z = (sizeof(void*) + 8) * zptr.size();
+  auto buf = dev_alloc(be, b_nodes + b_modes + b_levels + b_z + b_lists + 64, &rc);
+  OM_TRY(rc);
+  char* base = (char*)buf.get();
+  SpNode* d_nodes = (SpNode*)base;
+  SpMode* d_modes = (SpMode*)(base + b_nodes);
+  int* d_levels = (int*)(base + b_nodes + b_modes);
+  void** d_zptr = (void**)(((uintptr_t)(base + b_nodes + b_modes + b_levels) + 15) & ~(uintptr_t)15);
+  int64_t* d_zsize = (int64_t*)(d_zptr + zptr.size());
+  int64_t* d_lists = (int64_t*)(((uintptr_t)(d_zsize + zsize.size()) + 15) & ~(uintptr_t)15);
+  std::vector<char> host(b_nodes + b_modes + b_levels);
+  memcpy(host.data(), recs.data(), b_nodes);
+  if (b_modes) memcpy(host.data() + b_nodes, modes.data(), b_modes);
+  memcpy(host.data() + b_nodes + b_modes, level_start.data(), b_levels);
+  OM_CUDA(cudaMemcpyAsync(base, host.data(), host.size(), cudaMemcpyHostToDevice, be->stream),
+          "sparse backward upload");
+  if (!zptr.empty()) {
+    OM_CUDA(cudaMemcpyAsync(d_zptr, zptr.data(), sizeof(void*) * zptr.size(), cudaMemcpyHostToDevice,
+                            be->stream),
+            "sparse backward upload");
+    OM_CUDA(cudaMemcpyAsync(d_zsize, zsize.data(), 8 * zsize.size(), cudaMemcpyHostToDevice,
+                            be->stream),
+            "sparse backward upload");
+  }
+  auto val = dev_alloc(be, es * (size_t)std::max<int64_t>(n, 1), &rc);
+  OM_TRY(rc);
+  OM_CUDA(cudaMemcpyAsync(val.get(), dy, es * (size_t)n, cudaMemcpyDeviceToDevice, be->stream),
+          "grad copy");
+  ProfScope prof(be, "sparse_backward");
+  const int nz = (int)zptr.size();
+  if (dt == OM_F32) {
+    if (nz) zero_many_kernel<float><<<std::min(nz, be->num_sms * 4), 256, 0, be->stream>>>(
+        (float* const*)d_zptr, d_zsize, nz);
+    sparse_backward_kernel<float><<<1, 512, 0, be->stream>>>(
+        d_nodes, d_modes, d_levels, (int)level_start.size() - 1, 0, d_lists,
+        (const float*)val.get(), n);
+  } else {
+    if (nz) zero_many_kernel<double><<<std::min(nz, be->num_sms * 4), 256, 0, be->stream>>>(
+        (double* const*)d_zptr, d_zsize, nz);
+    sparse_backward_kernel<double><<<1, 512, 0, be->stream>>>(
+        d_nodes, d_modes, d_levels, (int)level_start.size() - 1, 0, d_lists,
+        (const double*)val.get(), n);
+  }
+  note_launch(nz ? 2 : 1);
+  return check_cuda(cudaGetLastError(), "sparse backward launch");
+}
 
 int Engine::backprop(int idx, const DTensor& dy, void* const* grads) {
   TapeNode& n = nodes[idx];
@@ -421,6 +623,8 @@ extern "C" int om_b200_einsum_backward(om_tape* tape, const void* dy, void* cons
   DTensor d = E.nodes[E.root].content;
   d.owner.reset();
   d.ptr = dy;
+  const int64_t n = d.numel();
+  if (E.tropical && n <= kSparseGradMax) return E.backprop_sparse(dy, grads);
   return E.backprop(E.root, d, grads);
 }
 
