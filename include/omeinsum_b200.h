@@ -176,6 +176,30 @@ int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, int ntensors,
 int om_b200_einsum_backward(om_tape* tape, const void* dy, void* const* grads);
 int om_b200_tape_free(om_tape* tape);
 
+/* For a tape recorded inside a graph (om_b200_graph_begin/end): frees the
+ * device buffers the tape refers to, stream-ordered, and keeps the tape.  A
+ * later replay of the graph allocates the same addresses again, after which
+ * om_b200_einsum_backward may run on the tape once more.  This keeps a
+ * recorded tape from holding its memory between replays.  Not meant for
+ * tapes made outside a graph (their buffers would not come back). */
+int om_b200_tape_release(om_tape* tape);
+
+/* Stream capture into a CUDA graph.  No counterpart in the reference (its
+ * CPU backend has no launch cost to amortise); it serves callers that repeat
+ * the same sequence of library calls on the same buffers, such as the slices
+ * of a sliced network.  Between om_b200_graph_begin and om_b200_graph_end,
+ * work issued on the backend's stream (om_b200_contract, om_b200_einsum,
+ * copies, ...) is recorded instead of run; the library's own stream-ordered
+ * allocations inside become part of the graph.  om_b200_graph_launch runs the
+ * recorded work on the backend's stream.  Calls that wait for the device
+ * (om_b200_sync, om_b200_download, profile queries) must not be made while
+ * capturing. */
+typedef struct om_graph om_graph;
+int om_b200_graph_begin(om_backend* be);
+int om_b200_graph_end(om_backend* be, om_graph** graph_out);
+int om_b200_graph_launch(om_backend* be, om_graph* graph);
+int om_b200_graph_free(om_graph* graph);
+
 /* Allocation-free tropical matrix product with argmax.  No counterpart in the
  * reference: it exists for callers that must not allocate device memory
  * while they run (a host that hands all device memory out of its own arena,

@@ -37,7 +37,8 @@ EXPORTS = [
     "om_b200_copy_strided", "om_b200_contract", "om_b200_unary", "om_b200_tropical_backward",
     "om_b200_launch_count", "om_b200_profile_enable", "om_b200_profile_query",
     "om_b200_tropical_matmul_argmax_noalloc", "om_b200_einsum", "om_b200_einsum_backward",
-    "om_b200_tape_free",
+    "om_b200_tape_free", "om_b200_graph_begin", "om_b200_graph_end", "om_b200_graph_launch",
+    "om_b200_graph_free", "om_b200_tape_release",
 ]
 
 
@@ -81,6 +82,10 @@ def lib():
         L.om_b200_unary.argtypes = [P, I, I, P, I, P, P, P, I, P, P, P, P]
         L.om_b200_tropical_backward.argtypes = [P, I, P, P, I, P, P, I, P, P, I, P, P, P, P]
         L.om_b200_launch_count.restype = I64
+        L.om_b200_graph_begin.argtypes = [P]
+        L.om_b200_graph_end.argtypes = [P, ctypes.POINTER(P)]
+        L.om_b200_graph_launch.argtypes = [P, P]
+        L.om_b200_graph_free.argtypes = [P]
         L.om_b200_profile_enable.argtypes = [P, I]
         L.om_b200_profile_query.argtypes = [P, I, ctypes.c_char_p, SZ,
                                             ctypes.POINTER(ctypes.c_double),
@@ -125,6 +130,24 @@ def col_strides(shape):
 def launch_count() -> int:
     """Device kernels launched by this thread since the last call."""
     return int(lib().om_b200_launch_count())
+
+
+class Graph:
+    """Recorded stream work (om_b200_graph_*); launch() replays it."""
+
+    def __init__(self, be, handle):
+        self.be, self.h = be, handle
+
+    def launch(self):
+        _check(lib().om_b200_graph_launch(self.be.h, self.h))
+
+    def __del__(self):
+        if getattr(self, "h", None) and lib is not None:
+            try:
+                lib().om_b200_graph_free(self.h)
+            except Exception:
+                pass
+            self.h = None
 
 
 class Storage:
@@ -194,6 +217,16 @@ class B200:
         _check(lib().om_b200_stream(self.h, ctypes.byref(s)))
         return s.value or 0
 
+    def graph_begin(self):
+        """Start recording the work issued on this backend's stream."""
+        _check(lib().om_b200_graph_begin(self.h))
+
+    def graph_end(self) -> "Graph":
+        """Stop recording; the recorded work as a replayable graph."""
+        g = ctypes.c_void_p()
+        _check(lib().om_b200_graph_end(self.h, ctypes.byref(g)))
+        return Graph(self, g.value)
+
     def profile(self, on: bool = True):
         """Turn per-kernel CUDA-event timing on (clearing it) or off."""
         _check(lib().om_b200_profile_enable(self.h, 1 if on else 0))
@@ -228,10 +261,13 @@ class B200:
     def copy_strided(self, src: Storage, shape, strides, offset=0) -> Storage:
         n = int(np.prod(shape)) if len(shape) else 1
         dst = self.alloc(n, src.dtype)
+        self.copy_strided_into(src, shape, strides, offset, dst)
+        return dst
+
+    def copy_strided_into(self, src: Storage, shape, strides, offset, dst: Storage):
         sh, st = _i64(shape), _i64(strides)
         _check(lib().om_b200_copy_strided(self.h, DTYPES[src.dtype], src.ptr, len(sh), _p(sh),
                                           _p(st), offset, dst.ptr))
-        return dst
 
     def contract_into(self, alg, a: Storage, shape_a, strides_a, modes_a, b: Storage, shape_b,
                       strides_b, modes_b, shape_c, modes_c, c: Storage, argmax: Storage | None):

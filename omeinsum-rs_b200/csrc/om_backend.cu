@@ -229,3 +229,49 @@ int om_b200_download(om_backend* be, void* dst, const void* src, size_t bytes) {
 }
 
 }  // extern "C"
+
+struct om_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+extern "C" int om_b200_graph_begin(om_backend* be) {
+  using namespace om;
+  if (!be) return set_error(OM_ERR_INVALID, "om_b200_graph_begin: null backend");
+  OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  // relaxed: the library may query or set function attributes while recording
+  OM_CUDA(cudaStreamBeginCapture(be->stream, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture");
+  return OM_OK;
+}
+
+extern "C" int om_b200_graph_end(om_backend* be, om_graph** graph_out) {
+  using namespace om;
+  if (!be || !graph_out) return set_error(OM_ERR_INVALID, "om_b200_graph_end: null argument");
+  OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  cudaGraph_t g = nullptr;
+  OM_CUDA(cudaStreamEndCapture(be->stream, &g), "cudaStreamEndCapture");
+  cudaGraphExec_t x = nullptr;
+  cudaError_t e = cudaGraphInstantiateWithFlags(&x, g, cudaGraphInstantiateFlagAutoFreeOnLaunch);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(g);
+    return check_cuda(e, "cudaGraphInstantiate");
+  }
+  *graph_out = new om_graph{g, x};
+  return OM_OK;
+}
+
+extern "C" int om_b200_graph_launch(om_backend* be, om_graph* graph) {
+  using namespace om;
+  if (!be || !graph) return set_error(OM_ERR_INVALID, "om_b200_graph_launch: null argument");
+  OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  OM_CUDA(cudaGraphLaunch(graph->exec, be->stream), "cudaGraphLaunch");
+  return OM_OK;
+}
+
+extern "C" int om_b200_graph_free(om_graph* graph) {
+  if (!graph) return OM_OK;
+  if (graph->exec) cudaGraphExecDestroy(graph->exec);
+  if (graph->graph) cudaGraphDestroy(graph->graph);
+  delete graph;
+  return OM_OK;
+}

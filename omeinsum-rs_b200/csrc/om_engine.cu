@@ -75,6 +75,7 @@ struct TapeNode {
   Op op;
   DTensor content;
   std::shared_ptr<void> argmax;  // u32, shaped like content (tropical)
+  const uint32_t* am = nullptr;  // argmax's address (kept when a recorded tape releases memory)
   int tensor_index = -1;         // Leaf
   std::vector<int32_t> in_ix, out_ix;        // Unary
   std::vector<int32_t> left_ix, right_ix;    // Binary (out_ix too)
@@ -307,6 +308,7 @@ struct Engine {
     n.out_ix = oix;
     n.child0 = child;
     OM_TRY(unary(nodes[child].content, oix, keep && tropical, n.content, n.argmax));
+    n.am = (const uint32_t*)n.argmax.get();
     nodes.push_back(std::move(n));
     *out_node = (int)nodes.size() - 1;
     return OM_OK;
@@ -364,12 +366,12 @@ int Engine::backprop_sparse(const void* dy, void* const* grads) {
     } else if (t.op == Op::Unary) {
       r.kind = 1;
       r.child0 = slot[t.child0];
-      r.argmax = (const uint32_t*)t.argmax.get();
+      r.argmax = t.am;
     } else {
       r.kind = 2;
       r.child0 = slot[t.child0];
       r.child1 = slot[t.child1];
-      r.argmax = (const uint32_t*)t.argmax.get();
+      r.argmax = t.am;
       r.off = (int)modes.size();
       const DTensor& l = nodes[t.child0].content;
       const DTensor& rr = nodes[t.child1].content;
@@ -474,10 +476,10 @@ int Engine::backprop(int idx, const DTensor& dy, void* const* grads) {
         ProfScope prof(be, "unary_scatter");
         if (dt == OM_F32)
           scatter_add_kernel<float><<<blocks, 256, 0, be->stream>>>(
-              (const float*)dy.ptr, (const uint32_t*)n.argmax.get(), (float*)g.ptr, cnt);
+              (const float*)dy.ptr, n.am, (float*)g.ptr, cnt);
         else
           scatter_add_kernel<double><<<blocks, 256, 0, be->stream>>>(
-              (const double*)dy.ptr, (const uint32_t*)n.argmax.get(), (double*)g.ptr, cnt);
+              (const double*)dy.ptr, n.am, (double*)g.ptr, cnt);
         note_launch();
         OM_CUDA(cudaGetLastError(), "scatter launch");
       }
@@ -497,7 +499,7 @@ int Engine::backprop(int idx, const DTensor& dy, void* const* grads) {
     OM_TRY(new_tensor(n.right_ix, gr));
     OM_CUDA(cudaMemsetAsync((void*)gl.ptr, 0, es * (size_t)gl.numel(), be->stream), "memset");
     OM_CUDA(cudaMemsetAsync((void*)gr.ptr, 0, es * (size_t)gr.numel(), be->stream), "memset");
-    OM_TRY(om_b200_tropical_backward(be, dt, dy.ptr, (const uint32_t*)n.argmax.get(),
+    OM_TRY(om_b200_tropical_backward(be, dt, dy.ptr, n.am,
                                      (int)n.left_ix.size(), l.shape.data(), n.left_ix.data(),
                                      (int)n.right_ix.size(), r.shape.data(), n.right_ix.data(),
                                      (int)n.out_ix.size(), dy.shape.data(), n.out_ix.data(),
@@ -600,6 +602,7 @@ extern "C" int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, in
       n.out_ix = E.node_order(E.nodes[l].content, E.nodes[r].content, niy_);
       OM_TRY(E.contract(E.nodes[l].content, n.left_ix, E.nodes[r].content, n.right_ix, n.out_ix,
                         E.keep && E.tropical, n.content, n.argmax));
+      n.am = (const uint32_t*)n.argmax.get();
       E.nodes.push_back(std::move(n));
       node_of[i] = (int)E.nodes.size() - 1;
     }
@@ -630,5 +633,16 @@ extern "C" int om_b200_einsum_backward(om_tape* tape, const void* dy, void* cons
 
 extern "C" int om_b200_tape_free(om_tape* tape) {
   delete tape;
+  return OM_OK;
+}
+
+extern "C" int om_b200_tape_release(om_tape* tape) {
+  if (!tape) return set_error(OM_ERR_INVALID, "om_b200_tape_release: null tape");
+  Engine& E = tape->eng;
+  OM_CUDA(cudaSetDevice(E.be->device), "cudaSetDevice");
+  for (auto& n : E.nodes) {
+    n.content.owner.reset();  // stream-ordered free; the address is kept
+    n.argmax.reset();
+  }
   return OM_OK;
 }

@@ -28,6 +28,7 @@ def _bind():
                                      ctypes.POINTER(P)]
         L.om_b200_einsum_backward.argtypes = [P, P, P]
         L.om_b200_tape_free.argtypes = [P]
+        L.om_b200_tape_release.argtypes = [P]
         L._einsum_bound = True
     return L
 
@@ -208,6 +209,28 @@ class Einsum:
 
     def call_views(self, be: B200, alg, tensors, views, out, tape):
         self._call(be, alg, tensors, out, tape, views)
+
+    def forward_tape_views(self, be: B200, alg, tensors, views, out) -> ctypes.c_void_p:
+        """Forward over strided views keeping the gradient tape; returns the
+        tape handle (free it with tape_free).  May be called while the
+        backend records a graph: the tape then refers to the graph's buffers
+        and stays valid across replays."""
+        tape = ctypes.c_void_p()
+        self._call(be, alg, tensors, out, ctypes.byref(tape), views)
+        return tape
+
+    @staticmethod
+    def backward_tape(tape, d: Storage, grads):
+        ptrs = (ctypes.c_void_p * len(grads))(*[g.ptr for g in grads])
+        _check(_bind().om_b200_einsum_backward(tape, d.ptr, ptrs))
+
+    @staticmethod
+    def tape_free(tape):
+        _bind().om_b200_tape_free(tape)
+
+    @staticmethod
+    def tape_release(tape):
+        _check(_bind().om_b200_tape_release(tape))
 
     def cost_and_gradient_views(self, be: B200, alg, tensors, views, dy):
         """cost_and_gradient over strided views; gradients are contiguous in

@@ -94,16 +94,24 @@ class DeviceExecutor:
     intermediate in every slice; value() contracts each such maximal subtree
     once, keeps the result on the device and feeds it to every slice as a
     leaf of a reduced tree, so a slice only runs the nodes that depend on
-    the sliced labels.  value_and_grad() runs the full tree (its gradient
-    flows to the original leaves)."""
+    the sliced labels.  The reduced contraction of the first slice is
+    recorded as a CUDA graph (om_b200_graph_*) and replayed for the others,
+    after their sliced leaves are copied into fixed staging buffers, so a
+    slice costs one graph launch instead of one host call per node.
+    value_and_grad() runs the full tree (its gradient flows to the original
+    leaves); its forward with tape is recorded the same way, the tape kept
+    across replays, and the backward runs after each replay."""
 
-    def __init__(self, be, E, alg, ixs, iy, sizes, tensors, tree):
+    def __init__(self, be, E, alg, ixs, iy, sizes, tensors, tree, use_graph=True):
         self.be, self.E, self.alg = be, E, alg
         self.ixs, self.iy, self.sizes, self.tree = ixs, iy, sizes, tree
         self.dev = [be.from_slice(t) for t in tensors]
         self.dtype = tensors[0].dtype
         self.enc = E.encode_tree(tree, ixs, iy) if not isinstance(tree, int) else ([], [])
         self._reduced = {}
+        self._plans = {}
+        self._grad_plans = {}
+        self.use_graph = use_graph
 
     def _einsum(self, assign):
         views = sliced_views(self.ixs, self.sizes, assign)
@@ -155,33 +163,138 @@ class DeviceExecutor:
         self._reduced[key] = (leaves, ixs, enc)
         return self._reduced[key]
 
-    def value(self, assign):
-        leaves, ixs, (children, node_iys) = self._reduce(assign.keys())
-        full = sliced_views(self.ixs, self.sizes, assign)
-        views, tensors = [], []
+    def _plan(self, assign):
+        """Fixed buffers and the reduced einsum for this set of sliced labels:
+        a leaf that carries a sliced label reads a staging buffer that every
+        slice refills, so the same recorded graph serves all slices."""
+        key = frozenset(assign.keys())
+        leaves, ixs, (children, node_iys) = self._reduce(key)
+        views, tensors, stage = [], [], []
+
+        def col(shape):
+            st, s = [], 1
+            for d in shape:
+                st.append(s)
+                s *= d
+            return st
         for lf in leaves:
             if lf[0] == "leaf":
-                views.append(full[lf[1]])
-                tensors.append(self.dev[lf[1]])
+                i = lf[1]
+                if set(self.ixs[i]) & key:
+                    vix = [l for l in self.ixs[i] if l not in key]
+                    shape = [self.sizes[l] for l in vix]
+                    buf = self.be.alloc(max(1, int(np.prod(shape))), self.dtype)
+                    stage.append((i, buf))
+                    views.append((0, shape, col(shape), vix))
+                    tensors.append(buf)
+                else:
+                    shape = [self.sizes[l] for l in self.ixs[i]]
+                    views.append((0, shape, col(shape), list(self.ixs[i])))
+                    tensors.append(self.dev[i])
             else:
                 shape = [self.sizes[l] for l in lf[2]]
-                st, s = [], 1
-                for d in shape:
-                    st.append(s)
-                    s *= d
-                views.append((0, shape, st, lf[2]))
+                views.append((0, shape, col(shape), lf[2]))
                 tensors.append(lf[1])
-        sizes = {l: v for l, v in self.sizes.items() if l not in assign}
-        node_iys = [[l for l in x if l not in assign] for x in node_iys]
+        sizes = {l: v for l, v in self.sizes.items() if l not in key}
+        node_iys = [[l for l in x if l not in key] for x in node_iys]
         ein = self.E.Einsum([v[3] for v in views], self.iy, sizes).set_encoded(children, node_iys)
         out = self.be.alloc(ein.out_size(), self.dtype)
-        ein.call_views(self.be, self.alg, tensors, views, out, None)
-        return float(out.to_vec()[0])
+        return {"ein": ein, "views": views, "tensors": tensors, "stage": stage, "out": out,
+                "graph": None}
+
+    def _stage(self, plan, assign):
+        full = sliced_views(self.ixs, self.sizes, assign)
+        for i, buf in plan["stage"]:
+            off, shape, st, _ = full[i]
+            self.be.copy_strided_into(self.dev[i], shape, st, off, buf)
+
+    def value(self, assign):
+        key = frozenset(assign.keys())
+        plan = self._plans.get(key)
+        if plan is None:
+            plan = self._plans[key] = self._plan(assign)
+            if self.use_graph:
+                # record one slice's contraction once; every slice replays it
+                self.be.graph_begin()
+                try:
+                    plan["ein"].call_views(self.be, self.alg, plan["tensors"], plan["views"],
+                                           plan["out"], None)
+                finally:
+                    plan["graph"] = self.be.graph_end()
+        self._stage(plan, assign)
+        if plan["graph"] is not None:
+            plan["graph"].launch()
+        else:
+            plan["ein"].call_views(self.be, self.alg, plan["tensors"], plan["views"], plan["out"],
+                                   None)
+        return float(plan["out"].to_vec()[0])
+
+    def _grad_plan(self, assign):
+        """The full tree over fixed buffers (sliced leaves read the staging
+        buffers of the value plan), its forward with tape recorded once as a
+        graph; the tape stays valid across replays."""
+        key = frozenset(assign.keys())
+        gp = self._grad_plans.get(key)
+        if gp is not None:
+            return gp
+        plan = self._plans.get(key) or self._plans.setdefault(key, self._plan(assign))
+        staged = dict(plan["stage"])
+        views, tensors = [], []
+        full = sliced_views(self.ixs, self.sizes, assign)
+        for i, (off, shape, st, vix) in enumerate(full):
+            if i in staged:
+                cs, s = [], 1
+                for d in shape:
+                    cs.append(s)
+                    s *= d
+                views.append((0, shape, cs, vix))
+                tensors.append(staged[i])
+            else:
+                views.append((off, shape, st, vix))
+                tensors.append(self.dev[i])
+        ein, _ = self._einsum(assign)
+        out = self.be.alloc(ein.out_size(), self.dtype)
+        grads = [self.be.alloc(max(1, int(np.prod(v[1]))), self.dtype) for v in views]
+        gp = {"ein": ein, "views": views, "tensors": tensors, "out": out, "grads": grads,
+              "graph": None, "tape": None, "plan": plan}
+        if self.use_graph:
+            self._stage(plan, assign)
+            self.be.graph_begin()
+            try:
+                gp["tape"] = ein.forward_tape_views(self.be, self.alg, tensors, views, out)
+            finally:
+                gp["graph"] = self.be.graph_end()
+            # recording ran nothing: the tape's buffers exist from the first
+            # replay on
+        self._grad_plans[key] = gp
+        return gp
 
     def value_and_grad(self, assign, dy=1.0):
-        ein, views = self._einsum(assign)
-        c, grads = ein.cost_and_gradient_views(self.be, self.alg, self.dev, views, [dy])
-        return float(c.to_vec()[0]), [g.to_vec() for g in grads]
+        gp = self._grad_plan(assign)
+        self._stage(gp["plan"], assign)
+        if gp["graph"] is not None:
+            gp["graph"].launch()
+            tape = gp["tape"]
+        else:
+            tape = gp["ein"].forward_tape_views(self.be, self.alg, gp["tensors"], gp["views"],
+                                                gp["out"])
+        try:
+            d = self.be.from_slice(np.asarray([dy], self.dtype))
+            gp["ein"].backward_tape(tape, d, gp["grads"])
+        finally:
+            if gp["graph"] is None:
+                gp["ein"].tape_free(tape)
+            else:  # the next replay brings the buffers back
+                gp["ein"].tape_release(tape)
+        return float(gp["out"].to_vec()[0]), [g.to_vec() for g in gp["grads"]]
+
+    def __del__(self):
+        for gp in getattr(self, "_grad_plans", {}).values():
+            if gp.get("tape") is not None:
+                try:
+                    gp["ein"].tape_free(gp["tape"])
+                except Exception:
+                    pass
 
 
 class OracleExecutor:
