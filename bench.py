@@ -202,13 +202,14 @@ def run_permuted(be, om, local_rank):
 
 
 NET_N = 190
-NET_SLICED = int(os.environ.get("OM_BENCH_NET_SLICED", "3"))
+NET_SLICED = int(os.environ.get("OM_BENCH_NET_SLICED", "6"))
 
 
 def run_network(be, om, world, rank, local_rank, args):
     """BASELINE config 4's method: MIS on a seeded 3-regular graph, MaxPlus
-    f32, 3 sliced labels (8 slices) spread over the ranks, combined by an
-    NCCL max-all-reduce carrying the slice id, then the argmax backward of the
+    f32, NET_SLICED sliced labels (2^NET_SLICED slices, 64 by default, so
+    every rank has 8 at N = 8) spread over the ranks, combined by an NCCL
+    max-all-reduce carrying the slice id, then the argmax backward of the
     winning slice (the configuration) broadcast.  n = 190 is the largest graph
     whose slices fit (n = 250 needs ~2^41 elements per intermediate)."""
     import importlib

@@ -185,6 +185,21 @@ class Storage:
             pass
 
 
+class View(Storage):
+    """A non-owning window into another Storage (freed with its parent)."""
+
+    def __init__(self, parent: Storage, offset: int, n: int):
+        super().__init__(parent.backend, parent.ptr + offset * parent.dtype.itemsize, n,
+                         parent.dtype)
+        self.parent = parent
+
+    def free(self):
+        self.ptr = None
+
+    def __del__(self):
+        pass
+
+
 class B200:
     """The B200 backend: `impl Backend for B200` in the reference's terms."""
 
@@ -263,6 +278,12 @@ class B200:
         dst = self.alloc(n, src.dtype)
         self.copy_strided_into(src, shape, strides, offset, dst)
         return dst
+
+    def copy_device(self, dst_ptr: int, src_ptr: int, nbytes: int):
+        """Stream-ordered device-to-device copy of nbytes."""
+        one = _i64([nbytes // 4])
+        unit = _i64([1])
+        _check(lib().om_b200_copy_strided(self.h, 2, src_ptr, 1, _p(one), _p(unit), 0, dst_ptr))
 
     def copy_strided_into(self, src: Storage, shape, strides, offset, dst: Storage):
         sh, st = _i64(shape), _i64(strides)

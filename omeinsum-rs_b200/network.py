@@ -23,6 +23,7 @@ logic on CPU ranks (gloo).
 from __future__ import annotations
 
 import itertools
+import sys
 
 import numpy as np
 
@@ -98,9 +99,10 @@ class DeviceExecutor:
     recorded as a CUDA graph (om_b200_graph_*) and replayed for the others,
     after their sliced leaves are copied into fixed staging buffers, so a
     slice costs one graph launch instead of one host call per node.
-    value_and_grad() runs the full tree (its gradient flows to the original
-    leaves); its forward with tape is recorded the same way, the tape kept
-    across replays, and the backward runs after each replay."""
+    value_and_grad() runs the reduced tree with a tape (recorded the same
+    way, the tape kept across replays); its gradient reaches the original
+    leaves directly or through the tapes the hoisted subtrees were
+    contracted with."""
 
     def __init__(self, be, E, alg, ixs, iy, sizes, tensors, tree, use_graph=True):
         self.be, self.E, self.alg = be, E, alg
@@ -111,19 +113,13 @@ class DeviceExecutor:
         self._reduced = {}
         self._plans = {}
         self._grad_plans = {}
+        self._sub_tapes = []
         self.use_graph = use_graph
-
-    def _einsum(self, assign):
-        views = sliced_views(self.ixs, self.sizes, assign)
-        sizes = {l: v for l, v in self.sizes.items() if l not in assign}
-        children, node_iys = self.enc
-        node_iys = [[l for l in x if l not in assign] for x in node_iys]
-        ein = self.E.Einsum([v[3] for v in views], self.iy, sizes).set_encoded(children, node_iys)
-        return ein, views
 
     def _reduce(self, sliced):
         """(leaves, encoded reduced tree) for this set of sliced labels;
-        leaves are ('leaf', i) or ('hoisted', Storage, labels)."""
+        leaves are ('leaf', i) or ('hoisted', Storage, labels, tape, the
+        subtree's original leaves)."""
         key = frozenset(sliced)
         if key in self._reduced:
             return self._reduced[key]
@@ -152,8 +148,15 @@ class DeviceExecutor:
                 out_l = list(labels[id(t)])
                 ein = E.Einsum([self.ixs[i] for i in sub], out_l, self.sizes)
                 ein.set_contraction_tree(remap(t))
-                val = ein.execute(self.be, self.alg, [self.dev[i] for i in sub])
-                leaves.append(("hoisted", val, out_l))
+                val = self.be.alloc(ein.out_size(), self.dtype)
+                # forward with tape: the gradient later flows back through it
+                tape = ein.forward_tape_views(
+                    self.be, self.alg, [self.dev[i] for i in sub],
+                    [(0, [self.sizes[l] for l in self.ixs[i]],
+                      E._col([self.sizes[l] for l in self.ixs[i]]), list(self.ixs[i]))
+                     for i in sub], val)
+                self._sub_tapes.append((ein, tape))
+                leaves.append(("hoisted", val, out_l, tape, sub))
                 ixs.append(out_l)
                 return len(leaves) - 1
             return (rec(t[0]), rec(t[1]))
@@ -203,12 +206,39 @@ class DeviceExecutor:
                 "graph": None}
 
     def _stage(self, plan, assign):
-        full = sliced_views(self.ixs, self.sizes, assign)
-        for i, buf in plan["stage"]:
-            off, shape, st, _ = full[i]
-            self.be.copy_strided_into(self.dev[i], shape, st, off, buf)
+        """Copy the slice's view of every sliced leaf into its staging buffer
+        (view shapes and strides are fixed per plan; only offsets change)."""
+        if "stage_views" not in plan:
+            plan["stage_views"] = []
+            for i, buf in plan["stage"]:
+                shape = [self.sizes[l] for l in self.ixs[i]]
+                st, acc = [], 1
+                for d in shape:
+                    st.append(acc)
+                    acc *= d
+                fixed = [(l, t) for l, t in zip(self.ixs[i], st) if l in assign]
+                vs = [d for l, d in zip(self.ixs[i], shape) if l not in assign]
+                vst = [t for l, t in zip(self.ixs[i], st) if l not in assign]
+                plan["stage_views"].append((i, buf, fixed, vs, vst))
+        for i, buf, fixed, vs, vst in plan["stage_views"]:
+            off = sum(assign[l] * t for l, t in fixed)
+            self.be.copy_strided_into(self.dev[i], vs, vst, off, buf)
 
-    def value(self, assign):
+    def values(self, assigns):
+        """Values of several slices: each replay leaves its result in a slot
+        of one device array, read back once at the end, so the host queues
+        all slices without waiting for any."""
+        if not assigns:
+            return []
+        plan = self._ensure_plan(assigns[0])
+        res = self.be.alloc(len(assigns), self.dtype)
+        es = np.dtype(self.dtype).itemsize
+        for q, assign in enumerate(assigns):
+            self._run(plan, assign)
+            self.be.copy_device(res.ptr + q * es, plan["out"].ptr, es)
+        return [float(x) for x in res.to_vec()]
+
+    def _ensure_plan(self, assign):
         key = frozenset(assign.keys())
         plan = self._plans.get(key)
         if plan is None:
@@ -221,47 +251,60 @@ class DeviceExecutor:
                                            plan["out"], None)
                 finally:
                     plan["graph"] = self.be.graph_end()
+        return plan
+
+    def _run(self, plan, assign):
         self._stage(plan, assign)
         if plan["graph"] is not None:
             plan["graph"].launch()
         else:
             plan["ein"].call_views(self.be, self.alg, plan["tensors"], plan["views"], plan["out"],
                                    None)
+
+    def value(self, assign):
+        plan = self._ensure_plan(assign)
+        self._run(plan, assign)
         return float(plan["out"].to_vec()[0])
 
     def _grad_plan(self, assign):
-        """The full tree over fixed buffers (sliced leaves read the staging
-        buffers of the value plan), its forward with tape recorded once as a
-        graph; the tape stays valid across replays."""
+        """The reduced tree of the value plan (same fixed buffers), its
+        forward with tape recorded once as a graph; the tape stays valid
+        across replays.  Gradients reaching a hoisted leaf continue through
+        the tape its subtree was contracted with."""
         key = frozenset(assign.keys())
         gp = self._grad_plans.get(key)
         if gp is not None:
             return gp
-        plan = self._plans.get(key) or self._plans.setdefault(key, self._plan(assign))
-        staged = dict(plan["stage"])
-        views, tensors = [], []
-        full = sliced_views(self.ixs, self.sizes, assign)
-        for i, (off, shape, st, vix) in enumerate(full):
-            if i in staged:
-                cs, s = [], 1
-                for d in shape:
-                    cs.append(s)
-                    s *= d
-                views.append((0, shape, cs, vix))
-                tensors.append(staged[i])
-            else:
-                views.append((off, shape, st, vix))
-                tensors.append(self.dev[i])
-        ein, _ = self._einsum(assign)
+        plan = self._ensure_plan(assign)
+        ein = plan["ein"]
         out = self.be.alloc(ein.out_size(), self.dtype)
-        grads = [self.be.alloc(max(1, int(np.prod(v[1]))), self.dtype) for v in views]
-        gp = {"ein": ein, "views": views, "tensors": tensors, "out": out, "grads": grads,
+        # every gradient the call returns lives in one buffer, read back once:
+        # the reduced tree's leaves, then each hoisted subtree's leaves
+        leaves = self._reduce(key)[0]
+        om = sys.modules[type(self.be).__module__]
+        sizes_red = [max(1, int(np.prod(v[1]))) for v in plan["views"]]
+        sub_sizes = [[max(1, int(np.prod([self.sizes[l] for l in self.ixs[i]]))) for i in lf[4]]
+                     if lf[0] == "hoisted" else [] for lf in leaves]
+        total = sum(sizes_red) + sum(sum(x) for x in sub_sizes)
+        gbuf = self.be.alloc(total, self.dtype)
+        at, grads, sub_grads = 0, [], []
+        for n in sizes_red:
+            grads.append(om.View(gbuf, at, n))
+            at += n
+        for sz in sub_sizes:
+            row = []
+            for n in sz:
+                row.append(om.View(gbuf, at, n))
+                at += n
+            sub_grads.append(row)
+        gp = {"ein": ein, "out": out, "grads": grads, "sub_grads": sub_grads, "gbuf": gbuf,
               "graph": None, "tape": None, "plan": plan}
         if self.use_graph:
             self._stage(plan, assign)
             self.be.graph_begin()
             try:
-                gp["tape"] = ein.forward_tape_views(self.be, self.alg, tensors, views, out)
+                gp["tape"] = ein.forward_tape_views(self.be, self.alg, plan["tensors"],
+                                                    plan["views"], out)
             finally:
                 gp["graph"] = self.be.graph_end()
             # recording ran nothing: the tape's buffers exist from the first
@@ -271,12 +314,13 @@ class DeviceExecutor:
 
     def value_and_grad(self, assign, dy=1.0):
         gp = self._grad_plan(assign)
-        self._stage(gp["plan"], assign)
+        plan = gp["plan"]
+        self._stage(plan, assign)
         if gp["graph"] is not None:
             gp["graph"].launch()
             tape = gp["tape"]
         else:
-            tape = gp["ein"].forward_tape_views(self.be, self.alg, gp["tensors"], gp["views"],
+            tape = gp["ein"].forward_tape_views(self.be, self.alg, plan["tensors"], plan["views"],
                                                 gp["out"])
         try:
             d = self.be.from_slice(np.asarray([dy], self.dtype))
@@ -286,7 +330,23 @@ class DeviceExecutor:
                 gp["ein"].tape_free(tape)
             else:  # the next replay brings the buffers back
                 gp["ein"].tape_release(tape)
-        return float(gp["out"].to_vec()[0]), [g.to_vec() for g in gp["grads"]]
+        leaves = self._reduce(assign.keys())[0]
+        for lf, g, sg in zip(leaves, gp["grads"], gp["sub_grads"]):
+            if lf[0] == "hoisted":  # on through the hoisted subtree's tape
+                self.E.Einsum.backward_tape(lf[3], g, sg)
+        host = gp["gbuf"].to_vec()
+        out = [None] * len(self.ixs)
+        base = gp["gbuf"].ptr
+        es = np.dtype(self.dtype).itemsize
+        for lf, g, sg in zip(leaves, gp["grads"], gp["sub_grads"]):
+            if lf[0] == "leaf":
+                o = (g.ptr - base) // es
+                out[lf[1]] = host[o:o + g.n].copy()
+            else:
+                for i, v in zip(lf[4], sg):
+                    o = (v.ptr - base) // es
+                    out[i] = host[o:o + v.n].copy()
+        return float(gp["out"].to_vec()[0]), out
 
     def __del__(self):
         for gp in getattr(self, "_grad_plans", {}).values():
@@ -295,6 +355,11 @@ class DeviceExecutor:
                     gp["ein"].tape_free(gp["tape"])
                 except Exception:
                     pass
+        for ein, tape in getattr(self, "_sub_tapes", []):
+            try:
+                ein.tape_free(tape)
+            except Exception:
+                pass
 
 
 class OracleExecutor:
@@ -363,8 +428,11 @@ def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device
     if alg in ("maxplus", "minplus"):
         minimize = alg == "minplus"
         best = None
-        for s in mine:
-            v = executor.value(assigns[s])
+        if hasattr(executor, "values"):
+            vals = executor.values([assigns[s] for s in mine])
+        else:
+            vals = [executor.value(assigns[s]) for s in mine]
+        for s, v in zip(mine, vals):
             key = (order_key(v, minimize) << 32) | (0xFFFFFFFF - s)
             if best is None or key > best:
                 best = key
