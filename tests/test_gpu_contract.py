@@ -358,3 +358,29 @@ def test_node_batched_tiny_k(be, alg):
     check_case(be, alg, orc.ties(503, 4096 * 2, -4, 4), [4096, 2], [2, 1], ma,
                orc.ties(504, 2 * 3, -4, 4), [2, 3], [1, 2], mb, [4096, 3], mc,
                argmax=alg != "standard")
+
+
+@pytest.mark.gpu
+def test_graph_replay_of_contractions(be):
+    """om_b200_graph_*: contractions recorded once replay on new input data
+    with the same results as eager calls (tropical bit-exact)."""
+    m, k, n = 96, 70, 80
+    A, B = be.alloc(m * k), be.alloc(k * n)
+    C, AM = be.alloc(m * n), be.alloc(m * n, np.uint32)
+    L = load_pkg().lib()
+
+    def upload(dst, x):
+        x = np.ascontiguousarray(x, np.float32)
+        assert L.om_b200_upload(be.h, dst.ptr, x.ctypes.data, x.nbytes) == 0
+
+    be.graph_begin()
+    be.contract_into("maxplus", A, [m, k], [1, m], [0, 1], B, [k, n], [1, k], [1, 2], [m, n],
+                     [0, 2], C, AM)
+    g = be.graph_end()
+    for seed in (5, 6, 7):
+        a, b = orc.ties(seed, m * k, -5, 5), orc.ties(seed + 50, k * n, -5, 5)
+        upload(A, a)
+        upload(B, b)
+        g.launch()
+        rc, ram = orc.gemm("maxplus", a, b, m, k, n, argmax=True)
+        assert bits_equal(C.to_vec(), rc) and np.array_equal(AM.to_vec(), ram)
