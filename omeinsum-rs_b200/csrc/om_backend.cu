@@ -7,6 +7,8 @@
 // release threshold, so freed blocks are cached and reused without a device
 // synchronisation -- the device-side counterpart of the CPU ScratchPool
 // (src/backend/cpu/buffer_pool.rs:2-47).
+#include <mutex>
+#include <set>
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
@@ -76,14 +78,111 @@ static void resolve_pending(om_backend* be) {
 }
 
 Scratch::~Scratch() {
-  if (ptr && be) cudaFreeAsync(ptr, be->stream);
+  if (ptr && be) be_free(be, ptr);
 }
 
 int Scratch::alloc(om_backend* b, size_t bytes) {
   be = b;
   if (bytes == 0) bytes = 16;
-  OM_CUDA(cudaMallocAsync(&ptr, bytes, b->stream), "scratch cudaMallocAsync");
+  return be_alloc(b, bytes, &ptr);
+}
+
+// ---- arenas ------------------------------------------------------------------
+static std::mutex g_arena_mu;
+static std::set<Arena*> g_arenas;
+
+void arena_register(Arena* a) {
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  g_arenas.insert(a);
+}
+void arena_unregister(Arena* a) {
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  g_arenas.erase(a);
+}
+
+bool Arena::owns(const void* p) const {
+  for (auto& c : chunks)
+    if ((const char*)p >= c.first && (const char*)p < c.first + c.second) return true;
+  return false;
+}
+
+int Arena::alloc(size_t bytes, void** out) {
+  bytes = (bytes + 255) & ~size_t(255);
+  for (auto it = free_blocks.begin(); it != free_blocks.end(); ++it) {
+    if (it->second < bytes) continue;
+    char* p = it->first;
+    const size_t rest = it->second - bytes;
+    free_blocks.erase(it);
+    if (rest) free_blocks[p + bytes] = rest;
+    used[p] = bytes;
+    *out = p;
+    return OM_OK;
+  }
+  // grow: a new chunk of at least 64 MiB (plain cudaMalloc is allowed while
+  // recording; it is not stream work)
+  const size_t sz = std::max(bytes, size_t(64) << 20);
+  void* c = nullptr;
+  OM_CUDA(cudaMalloc(&c, sz), "arena cudaMalloc");
+  chunks.push_back({(char*)c, sz});
+  if (sz > bytes) free_blocks[(char*)c + bytes] = sz - bytes;
+  used[(char*)c] = bytes;
+  *out = c;
   return OM_OK;
+}
+
+void Arena::release(void* p) {
+  auto it = used.find((char*)p);
+  if (it == used.end()) return;
+  char* a = it->first;
+  size_t n = it->second;
+  used.erase(it);
+  char *lo = nullptr, *hi = nullptr;  // the chunk holding the block
+  for (auto& c : chunks)
+    if (a >= c.first && a < c.first + c.second) {
+      lo = c.first;
+      hi = c.first + c.second;
+    }
+  auto nx = free_blocks.lower_bound(a);
+  if (nx != free_blocks.end() && nx->first == a + n && nx->first < hi) {
+    n += nx->second;
+    free_blocks.erase(nx);
+  }
+  auto pv = free_blocks.lower_bound(a);
+  if (pv != free_blocks.begin()) {
+    --pv;
+    if (pv->first >= lo && pv->first + pv->second == a) {
+      pv->second += n;
+      return;
+    }
+  }
+  free_blocks[a] = n;
+}
+
+void Arena::destroy() {
+  for (auto& c : chunks) cudaFree(c.first);
+  chunks.clear();
+  free_blocks.clear();
+  used.clear();
+}
+
+int be_alloc(om_backend* be, size_t bytes, void** out) {
+  if (bytes == 0) bytes = 16;
+  if (be->recording) return be->recording->alloc(bytes, out);
+  OM_CUDA(cudaMallocAsync(out, bytes, be->stream), "cudaMallocAsync");
+  return OM_OK;
+}
+
+void be_free(om_backend* be, void* p) {
+  if (!p) return;
+  {
+    std::lock_guard<std::mutex> lk(g_arena_mu);
+    for (Arena* a : g_arenas)
+      if (a->owns(p)) {
+        a->release(p);
+        return;
+      }
+  }
+  cudaFreeAsync(p, be->stream);
 }
 
 }  // namespace om
@@ -233,14 +332,19 @@ int om_b200_download(om_backend* be, void* dst, const void* src, size_t bytes) {
 struct om_graph {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  om::Arena* arena = nullptr;  // the recorded work's buffers
 };
 
 extern "C" int om_b200_graph_begin(om_backend* be) {
   using namespace om;
   if (!be) return set_error(OM_ERR_INVALID, "om_b200_graph_begin: null backend");
   OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
-  // relaxed: the library may query or set function attributes while recording
+  if (be->recording) return set_error(OM_ERR_INVALID, "om_b200_graph_begin: already recording");
+  // relaxed: the library may set function attributes or grow its arena
+  // (cudaMalloc) while recording
   OM_CUDA(cudaStreamBeginCapture(be->stream, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture");
+  be->recording = new Arena();
+  arena_register(be->recording);
   return OM_OK;
 }
 
@@ -248,15 +352,29 @@ extern "C" int om_b200_graph_end(om_backend* be, om_graph** graph_out) {
   using namespace om;
   if (!be || !graph_out) return set_error(OM_ERR_INVALID, "om_b200_graph_end: null argument");
   OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  Arena* arena = be->recording;
+  be->recording = nullptr;
+  auto drop_arena = [&] {
+    if (arena) {
+      arena_unregister(arena);
+      arena->destroy();
+      delete arena;
+    }
+  };
   cudaGraph_t g = nullptr;
-  OM_CUDA(cudaStreamEndCapture(be->stream, &g), "cudaStreamEndCapture");
+  cudaError_t e = cudaStreamEndCapture(be->stream, &g);
+  if (e != cudaSuccess) {
+    drop_arena();
+    return check_cuda(e, "cudaStreamEndCapture");
+  }
   cudaGraphExec_t x = nullptr;
-  cudaError_t e = cudaGraphInstantiateWithFlags(&x, g, cudaGraphInstantiateFlagAutoFreeOnLaunch);
+  e = cudaGraphInstantiateWithFlags(&x, g, cudaGraphInstantiateFlagAutoFreeOnLaunch);
   if (e != cudaSuccess) {
     cudaGraphDestroy(g);
+    drop_arena();
     return check_cuda(e, "cudaGraphInstantiate");
   }
-  *graph_out = new om_graph{g, x};
+  *graph_out = new om_graph{g, x, arena};
   return OM_OK;
 }
 
@@ -272,6 +390,12 @@ extern "C" int om_b200_graph_free(om_graph* graph) {
   if (!graph) return OM_OK;
   if (graph->exec) cudaGraphExecDestroy(graph->exec);
   if (graph->graph) cudaGraphDestroy(graph->graph);
+  if (graph->arena) {
+    cudaDeviceSynchronize();  // a replay may still use the buffers
+    om::arena_unregister(graph->arena);
+    graph->arena->destroy();
+    delete graph->arena;
+  }
   delete graph;
   return OM_OK;
 }

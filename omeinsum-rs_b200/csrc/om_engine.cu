@@ -37,14 +37,9 @@ namespace {
 // device buffer freed on the backend's stream when the last owner goes
 std::shared_ptr<void> dev_alloc(om_backend* be, size_t bytes, int* rc) {
   void* p = nullptr;
-  cudaError_t e = cudaMallocAsync(&p, bytes ? bytes : 16, be->stream);
-  if (e != cudaSuccess) {
-    *rc = check_cuda(e, "engine cudaMallocAsync");
-    return nullptr;
-  }
-  *rc = OM_OK;
-  cudaStream_t s = be->stream;
-  return std::shared_ptr<void>(p, [s](void* q) { cudaFreeAsync(q, s); });
+  *rc = be_alloc(be, bytes ? bytes : 16, &p);
+  if (*rc != OM_OK) return nullptr;
+  return std::shared_ptr<void>(p, [be](void* q) { be_free(be, q); });
 }
 
 struct DTensor {

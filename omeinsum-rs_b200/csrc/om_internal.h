@@ -12,8 +12,15 @@
 
 #include "omeinsum_b200.h"
 
+namespace om {
+struct Arena;
+}
+
 struct om_backend {
   int device = 0;
+  // while a graph is being recorded, the library's own device memory comes
+  // from this arena (owned by the graph) instead of the stream-ordered pool
+  om::Arena* recording = nullptr;
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   // device flag word used by kernels that pick a path on the device
@@ -56,6 +63,29 @@ struct ProfScope {
 #define OM_CUDA(expr, what) OM_TRY(::om::check_cuda((expr), (what)))
 
 inline size_t dtype_size(om_dtype dt) { return dt == OM_F64 ? 8 : 4; }
+
+// ---- device memory of the library's own buffers --------------------------
+// Outside a recording: the device's stream-ordered pool (cudaMallocAsync /
+// cudaFreeAsync).  While a graph is recorded: a first-fit arena owned by the
+// graph, so the recorded work always finds its buffers at the same addresses
+// and different graphs never trade physical memory between replays (all
+// recorded work runs on one stream, in recording order, so reusing a freed
+// block inside the arena is safe).
+struct Arena {
+  std::vector<std::pair<char*, size_t>> chunks;
+  std::map<char*, size_t> free_blocks;  // address-ordered, coalesced
+  std::map<char*, size_t> used;
+  bool owns(const void* p) const;
+  int alloc(size_t bytes, void** out);
+  void release(void* p);
+  void destroy();
+};
+int be_alloc(om_backend* be, size_t bytes, void** out);
+// frees p: into the live arena that holds it, if any (a destroyed arena's
+// blocks are gone with it), else stream-ordered to the pool
+void be_free(om_backend* be, void* p);
+void arena_register(Arena* a);
+void arena_unregister(Arena* a);
 
 // ---- scratch memory (stream-ordered, cached by the device pool) -----------
 struct Scratch {
