@@ -374,7 +374,8 @@ def run_b200(args, rank, world, local_rank):
     achieved = OPS / (kms / kn / 1e3) / 1e12 if kn and kms else None
     threads_cpu = 1
     cpu_rows = int(os.environ.get("OM_BENCH_CPU_ROWS", str(M)))
-    cpu_val, cpu_dt = cpu_sample(threads_cpu, cpu_rows)
+    # the CPU baseline is an N = 1 figure; multi-GPU lines leave it out
+    cpu_val, cpu_dt = cpu_sample(threads_cpu, cpu_rows) if world == 1 else (None, None)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_max / args.steps, 4),
@@ -398,10 +399,10 @@ def run_b200(args, rank, world, local_rank):
                      else round(achieved / PAIR_CEILING_TOPS, 4),
                      "traffic": NCU_TRAFFIC_BYTES},
         "kernels": {k: {"ms_total": round(v[0], 4), "launches": v[1]} for k, v in prof.items()},
-        "cpu_baseline": {"value": round(cpu_val, 4), "unit": UNIT, "cores": threads_cpu,
-                         "kind": "port",
-                         "sample": f"rows 0..{cpu_rows - 1} of the workload (all columns, "
-                                   f"full k), reference loop order, {cpu_dt:.1f} s"},
+        "cpu_baseline": None if cpu_val is None else {
+            "value": round(cpu_val, 4), "unit": UNIT, "cores": threads_cpu, "kind": "port",
+            "sample": f"rows 0..{cpu_rows - 1} of the workload (all columns, full k), "
+                      f"reference loop order, {cpu_dt:.1f} s"},
         "clocks": clk.summary(),
         "network": network,
         "network_8_slices": network8,
