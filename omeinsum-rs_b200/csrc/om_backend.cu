@@ -88,8 +88,18 @@ int Scratch::alloc(om_backend* b, size_t bytes) {
 }
 
 // ---- arenas ------------------------------------------------------------------
-static std::mutex g_arena_mu;
-static std::set<Arena*> g_arenas;
+// Registries of live arenas and backends.  Never destroyed: buffers (a
+// tape's, a graph's) can be released during process teardown, after static
+// destructors would have run.
+static std::mutex& g_arena_mu = *new std::mutex;
+static std::set<Arena*>& g_arenas = *new std::set<Arena*>;
+static std::set<const om_backend*>& g_live = *new std::set<const om_backend*>;
+
+static void backend_live(const om_backend* be, bool on) {
+  std::lock_guard<std::mutex> lk(g_arena_mu);
+  if (on) g_live.insert(be);
+  else g_live.erase(be);
+}
 
 void arena_register(Arena* a) {
   std::lock_guard<std::mutex> lk(g_arena_mu);
@@ -181,6 +191,9 @@ void be_free(om_backend* be, void* p) {
         a->release(p);
         return;
       }
+    // a buffer that outlives its backend (a tape freed after
+    // om_b200_destroy) goes back with the device's pool at teardown
+    if (!g_live.count(be)) return;
   }
   cudaFreeAsync(p, be->stream);
 }
@@ -239,12 +252,14 @@ int om_b200_create(int device, om_backend** out) {
     delete be;
     return check_cuda(e, "cudaMalloc(flags)");
   }
+  backend_live(be, true);
   *out = be;
   return OM_OK;
 }
 
 int om_b200_destroy(om_backend* be) {
   if (!be) return OM_OK;
+  backend_live(be, false);
   cudaSetDevice(be->device);
   resolve_pending(be);
   cudaFree(be->d_flags);
