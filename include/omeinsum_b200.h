@@ -174,6 +174,18 @@ int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, int ntensors,
  * like the output, contiguous), writes the gradient of every input tensor t,
  * contiguous column-major in the input's shape, to grads[t]. */
 int om_b200_einsum_backward(om_tape* tape, const void* dy, void* const* grads);
+
+/* One backward through several tapes (no counterpart in the reference):
+ * input tensor link_leaf[i] of `tape` is the output of the contraction
+ * recorded in link_tapes[i] (same algebra and dtype, its output contiguous in
+ * that leaf's label order); the gradient continues through it, and the
+ * inputs of link_tapes[i] receive theirs in link_grads[i][...].  grads[] of
+ * linked leaves are not written.  Tropical tapes whose output has at most
+ * 4096 elements only (the walk of om_b200_einsum_backward for small
+ * gradients, in one launch for all tapes); otherwise OM_ERR_UNSUPPORTED. */
+int om_b200_einsum_backward_linked(om_tape* tape, const void* dy, void* const* grads, int nlinks,
+                                   const int32_t* link_leaf, om_tape* const* link_tapes,
+                                   void* const* const* link_grads);
 int om_b200_tape_free(om_tape* tape);
 
 /* For a tape recorded inside a graph (om_b200_graph_begin/end): frees the

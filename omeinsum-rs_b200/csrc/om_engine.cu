@@ -125,8 +125,8 @@ __global__ void __launch_bounds__(512) sparse_backward_kernel(const SpNode* __re
       if (nd.kind == 0) {
         const T v = val[e];
         if (v != T(0)) atomicAdd((T*)nd.grad + o, v);
-      } else if (nd.kind == 1) {
-        lists[(int64_t)nd.child0 * n + e] = nd.argmax[o];
+      } else if (nd.kind == 1) {  // unary, or a link into another tape (no argmax)
+        lists[(int64_t)nd.child0 * n + e] = nd.argmax ? (int64_t)nd.argmax[o] : o;
       } else {
         int64_t pa = 0, pb = 0, rem = o;
         const SpMode* m = modes + nd.off;
@@ -321,29 +321,53 @@ struct Engine {
 
   int backprop(int idx, const DTensor& dy, void* const* grads);
   int backprop_sparse(const void* dy, void* const* grads);
+  // the same walk over this tape and, through the leaves named in `link`
+  // (leaf tensor index -> tape), over further tapes whose roots are those
+  // leaves' contents; grads of tape k go to egrads[k]
+  int backprop_sparse_linked(const void* dy, const std::vector<const Engine*>& engines,
+                             const std::vector<void* const*>& egrads,
+                             const std::map<int, int>& link);
 };
 
 // Tropical backward for a small root gradient: the tape is laid out level
 // by level from the root and walked by sparse_backward_kernel in one launch.
 int Engine::backprop_sparse(const void* dy, void* const* grads) {
+  return backprop_sparse_linked(dy, {this}, {grads}, {});
+}
+
+int Engine::backprop_sparse_linked(const void* dy, const std::vector<const Engine*>& engines,
+                                   const std::vector<void* const*>& egrads,
+                                   const std::map<int, int>& link) {
   const int64_t n = nodes[root].content.numel();
-  std::vector<int> order{root}, level_start{0}, slot(nodes.size(), -1);
-  slot[root] = 0;
+  // breadth-first over (tape, node) from this tape's root
+  std::vector<std::pair<int, int>> order{{0, root}};
+  std::vector<std::vector<int>> slots(engines.size());
+  for (size_t k = 0; k < engines.size(); ++k) slots[k].assign(engines[k]->nodes.size(), -1);
+  slots[0][root] = 0;
+  std::vector<int> level_start{0};
+  auto visit = [&](int k, int c) {
+    if (c >= 0 && slots[k][c] < 0) {
+      slots[k][c] = (int)order.size();
+      order.push_back({k, c});
+    }
+  };
   for (size_t head = 0; head < order.size();) {
     const size_t end = order.size();
     level_start.push_back((int)end);
     for (; head < end; ++head) {
-      const TapeNode& t = nodes[order[head]];
-      for (int c : {t.child0, t.child1})
-        if (c >= 0 && t.op != Op::Leaf && slot[c] < 0) {
-          slot[c] = (int)order.size();
-          order.push_back(c);
-        }
+      const int k = order[head].first;
+      const TapeNode& t = engines[k]->nodes[order[head].second];
+      if (t.op == Op::Leaf) {
+        auto it = k == 0 ? link.find(t.tensor_index) : link.end();
+        if (it != link.end()) visit(it->second, engines[it->second]->root);
+        continue;
+      }
+      visit(k, t.child0);
+      visit(k, t.child1);
     }
     if (order.size() == end) break;
   }
   if (level_start.back() != (int)order.size()) level_start.push_back((int)order.size());
-  // drop a repeated final boundary
   while (level_start.size() >= 2 && level_start[level_start.size() - 2] == level_start.back())
     level_start.pop_back();
   std::vector<SpNode> recs(order.size());
@@ -351,11 +375,19 @@ int Engine::backprop_sparse(const void* dy, void* const* grads) {
   std::vector<void*> zptr;
   std::vector<int64_t> zsize;
   for (size_t q = 0; q < order.size(); ++q) {
-    const TapeNode& t = nodes[order[q]];
+    const int k = order[q].first;
+    const auto& enodes = engines[k]->nodes;
+    const TapeNode& t = enodes[order[q].second];
+    const std::vector<int>& slot = slots[k];
     SpNode r{};
-    if (t.op == Op::Leaf) {
+    auto lk = (k == 0 && t.op == Op::Leaf) ? link.find(t.tensor_index) : link.end();
+    if (lk != link.end()) {
+      r.kind = 1;  // identity into the linked tape's root
+      r.child0 = slots[lk->second][engines[lk->second]->root];
+      r.argmax = nullptr;
+    } else if (t.op == Op::Leaf) {
       r.kind = 0;
-      r.grad = grads[t.tensor_index];
+      r.grad = egrads[k][t.tensor_index];
       zptr.push_back(r.grad);
       zsize.push_back(t.content.numel());
     } else if (t.op == Op::Unary) {
@@ -368,8 +400,8 @@ int Engine::backprop_sparse(const void* dy, void* const* grads) {
       r.child1 = slot[t.child1];
       r.argmax = t.am;
       r.off = (int)modes.size();
-      const DTensor& l = nodes[t.child0].content;
-      const DTensor& rr = nodes[t.child1].content;
+      const DTensor& l = enodes[t.child0].content;
+      const DTensor& rr = enodes[t.child1].content;
       auto stride_in = [](const std::vector<int32_t>& ix, const std::vector<int64_t>& shape,
                           int32_t lab) -> int64_t {
         int64_t s = 1;
@@ -640,4 +672,32 @@ extern "C" int om_b200_tape_release(om_tape* tape) {
     n.argmax.reset();
   }
   return OM_OK;
+}
+
+extern "C" int om_b200_einsum_backward_linked(om_tape* tape, const void* dy, void* const* grads,
+                                              int nlinks, const int32_t* link_leaf,
+                                              om_tape* const* link_tapes,
+                                              void* const* const* link_grads) {
+  if (!tape || !dy || !grads || nlinks < 0 || (nlinks && (!link_leaf || !link_tapes || !link_grads)))
+    return set_error(OM_ERR_INVALID, "om_b200_einsum_backward_linked: null argument");
+  Engine& E = tape->eng;
+  OM_CUDA(cudaSetDevice(E.be->device), "cudaSetDevice");
+  if (!E.tropical || E.nodes[E.root].content.numel() > kSparseGradMax)
+    return set_error(OM_ERR_UNSUPPORTED,
+                     "om_b200_einsum_backward_linked: tropical tapes with a root of at most 4096 "
+                     "elements only");
+  std::vector<const Engine*> engines{&E};
+  std::vector<void* const*> egrads{grads};
+  std::map<int, int> link;
+  for (int i = 0; i < nlinks; ++i) {
+    if (!link_tapes[i] || !link_grads[i])
+      return set_error(OM_ERR_INVALID, "om_b200_einsum_backward_linked: null linked tape");
+    const Engine& S = link_tapes[i]->eng;
+    if (S.alg != E.alg || S.dt != E.dt)
+      return set_error(OM_ERR_INVALID, "om_b200_einsum_backward_linked: algebra or dtype differs");
+    link[link_leaf[i]] = (int)engines.size();
+    engines.push_back(&S);
+    egrads.push_back(link_grads[i]);
+  }
+  return E.backprop_sparse_linked(dy, engines, egrads, link);
 }

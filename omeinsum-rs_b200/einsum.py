@@ -29,6 +29,7 @@ def _bind():
         L.om_b200_einsum_backward.argtypes = [P, P, P]
         L.om_b200_tape_free.argtypes = [P]
         L.om_b200_tape_release.argtypes = [P]
+        L.om_b200_einsum_backward_linked.argtypes = [P, P, P, I, P, P, P]
         L._einsum_bound = True
     return L
 
@@ -223,6 +224,20 @@ class Einsum:
     def backward_tape(tape, d: Storage, grads):
         ptrs = (ctypes.c_void_p * len(grads))(*[g.ptr for g in grads])
         _check(_bind().om_b200_einsum_backward(tape, d.ptr, ptrs))
+
+    @staticmethod
+    def backward_tape_linked(tape, d: Storage, grads, links):
+        """links: [(leaf index of `tape`, tape of the contraction that made
+        that leaf, grads of that contraction's inputs)]; one launch walks all
+        tapes (tropical, small output only; raises OmError otherwise)."""
+        P = ctypes.c_void_p
+        ptrs = (P * len(grads))(*[g.ptr for g in grads])
+        leaf = _i32([l[0] for l in links])
+        tapes = (P * len(links))(*[l[1] for l in links])
+        rows = [(P * len(l[2]))(*[g.ptr for g in l[2]]) for l in links]
+        rowp = (P * len(links))(*[ctypes.cast(r, P) for r in rows])
+        _check(_bind().om_b200_einsum_backward_linked(tape, d.ptr, ptrs, len(links), _p(leaf),
+                                                      tapes, rowp))
 
     @staticmethod
     def tape_free(tape):

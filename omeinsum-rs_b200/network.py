@@ -322,18 +322,23 @@ class DeviceExecutor:
         else:
             tape = gp["ein"].forward_tape_views(self.be, self.alg, plan["tensors"], plan["views"],
                                                 gp["out"])
+        leaves = self._reduce(assign.keys())[0]
+        links = [(j, lf[3], sg) for j, (lf, sg) in enumerate(zip(leaves, gp["sub_grads"]))
+                 if lf[0] == "hoisted"]
         try:
             d = self.be.from_slice(np.asarray([dy], self.dtype))
-            gp["ein"].backward_tape(tape, d, gp["grads"])
+            try:  # one launch through the reduced tape and the hoisted ones
+                self.E.Einsum.backward_tape_linked(tape, d, gp["grads"], links)
+                links = []
+            except sys.modules[type(self.be).__module__].OmError:
+                gp["ein"].backward_tape(tape, d, gp["grads"])
         finally:
             if gp["graph"] is None:
                 gp["ein"].tape_free(tape)
             else:  # the next replay brings the buffers back
                 gp["ein"].tape_release(tape)
-        leaves = self._reduce(assign.keys())[0]
-        for lf, g, sg in zip(leaves, gp["grads"], gp["sub_grads"]):
-            if lf[0] == "hoisted":  # on through the hoisted subtree's tape
-                self.E.Einsum.backward_tape(lf[3], g, sg)
+        for j, sub_tape, sg in links:  # on through each hoisted subtree's tape
+            self.E.Einsum.backward_tape(sub_tape, gp["grads"][j], sg)
         host = gp["gbuf"].to_vec()
         out = [None] * len(self.ixs)
         base = gp["gbuf"].ptr
