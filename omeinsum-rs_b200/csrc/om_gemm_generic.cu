@@ -185,6 +185,10 @@ __device__ __forceinline__ void store_idx(uint32_t* p, const uint32_t (&v)[1]) {
 // contiguous (w = 4) and aligned, two 8/16-byte loads for two pairs (w = 2),
 // one load when all four coincide (w = 0, a broadcast operand), else scalar
 // loads.  Alignment is tested per group.
+// The V values of a group at p + off[i]: one 16-byte load when they are
+// contiguous (w = 4), two 8/16-byte loads for two pairs (w = 2), one load
+// when all four coincide (w = 0, a broadcast operand), else scalar loads.
+// The launcher grants w = 4 / 2 only when every group start is aligned.
 template <int V, typename T>
 __device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], int w,
                                            T (&out)[V]) {
@@ -193,7 +197,7 @@ __device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], 
       out[0] = out[1] = out[2] = out[3] = p[0];
       return;
     }
-    if (w == 4 && ((uintptr_t)p & (4 * sizeof(T) - 1)) == 0) {
+    if (w == 4) {
       if constexpr (sizeof(T) == 4) {
         const float4 v = *reinterpret_cast<const float4*>(p);
         out[0] = v.x, out[1] = v.y, out[2] = v.z, out[3] = v.w;
@@ -204,7 +208,7 @@ __device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], 
       }
       return;
     }
-    if (w >= 2 && (((uintptr_t)p | (uintptr_t)(p + off[2])) & (2 * sizeof(T) - 1)) == 0) {
+    if (w == 2) {
       if constexpr (sizeof(T) == 4) {
         const float2 v0 = *reinterpret_cast<const float2*>(p);
         const float2 v1 = *reinterpret_cast<const float2*>(p + off[2]);
@@ -224,19 +228,22 @@ __device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], 
 template <typename T, int ALG, bool ARGMAX, int KT, int V>
 __global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
   using S = Semi<ALG, T>;
-  __shared__ int64_t ka[kNodeKTable], kb[kNodeKTable];
-  __shared__ int64_t la[kNodeQuads], lb[kNodeQuads];
+  // four-output groups run on 32-bit offsets (the launcher checks that
+  // every offset of both operands fits); single outputs keep 64-bit ones
+  using Off = std::conditional_t<V == 4, int32_t, int64_t>;
+  __shared__ Off ka[kNodeKTable], kb[kNodeKTable];
+  __shared__ Off la[kNodeQuads], lb[kNodeQuads];
   const int tid = threadIdx.x;
   const bool ktab = g.K <= kNodeKTable;
   if (ktab)
     for (int k = tid; k < (int)g.K; k += blockDim.x) {
       uint32_t r = (uint32_t)k;
-      int64_t oa = 0, ob = 0;
+      Off oa = 0, ob = 0;
       for (int j = 0; j < g.nk; ++j) {
         const uint32_t q = fast_div(r, g.kmodes[j].div);
         const uint32_t d = r - q * g.kmodes[j].div.d;
-        oa += (int64_t)d * g.kmodes[j].sa;
-        ob += (int64_t)d * g.kmodes[j].sb;
+        oa += (Off)d * (Off)g.kmodes[j].sa;
+        ob += (Off)d * (Off)g.kmodes[j].sb;
         r = q;
       }
       ka[k] = oa;
@@ -245,12 +252,12 @@ __global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
   const int Q = g.P / V;  // groups of V outputs in a tile row
   for (int q0 = tid; q0 < Q; q0 += blockDim.x) {
     uint32_t r = (uint32_t)(q0 * V);
-    int64_t oa = 0, ob = 0;
+    Off oa = 0, ob = 0;
     for (int j = 0; j < g.nlow; ++j) {
       const uint32_t q = fast_div(r, g.out[j].div);
       const uint32_t d = r - q * g.out[j].div.d;
-      oa += (int64_t)d * g.out[j].sa;
-      ob += (int64_t)d * g.out[j].sb;
+      oa += (Off)d * (Off)g.out[j].sa;
+      ob += (Off)d * (Off)g.out[j].sb;
       r = q;
     }
     la[q0] = oa;
@@ -270,17 +277,17 @@ __global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
     const int64_t row = r0 + sub;
     if (row >= g.rows) break;
     uint32_t r = (uint32_t)row;
-    int64_t ha = 0, hb = 0;
+    Off ha = 0, hb = 0;
     for (int j = g.nlow; j < g.nout; ++j) {
       const uint32_t q = fast_div(r, g.out[j].div);
       const uint32_t d = r - q * g.out[j].div.d;
-      ha += (int64_t)d * g.out[j].sa;
-      hb += (int64_t)d * g.out[j].sb;
+      ha += (Off)d * (Off)g.out[j].sa;
+      hb += (Off)d * (Off)g.out[j].sb;
       r = q;
     }
     for (int q = q_first; q < Q; q += q_step) {
-      const T* a = A + ha + la[q];
-      const T* b = B + hb + lb[q];
+      const T* a = A + (int64_t)(ha + la[q]);
+      const T* b = B + (int64_t)(hb + lb[q]);
       T acc[V];
       uint32_t idx[V];
 #pragma unroll
@@ -447,8 +454,24 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
       if (pre > 4) break;
     }
   }
+  // groups of four use 32-bit offsets: every offset of A and B must fit
+  auto span_fits = [&](bool is_a) {
+    int64_t span = 0;
+    for (int j = 0; j < g.nout; ++j) {
+      const int64_t st = is_a ? g.out[j].sa : g.out[j].sb;
+      if (st < 0) return false;
+      span += (int64_t)(g.out[j].div.d - 1) * st;
+    }
+    for (int j = 0; j < g.nk; ++j) {
+      const int64_t st = is_a ? g.kmodes[j].sa : g.kmodes[j].sb;
+      if (st < 0) return false;
+      span += (int64_t)(g.kmodes[j].div.d - 1) * st;
+    }
+    return span < (int64_t(1) << 31);
+  };
   const bool v4 = sep && g.total % 4 == 0 && ((uintptr_t)g.C % (4 * es)) == 0 &&
-                  (!g.argmax || ((uintptr_t)g.argmax % 16) == 0);
+                  (!g.argmax || ((uintptr_t)g.argmax % 16) == 0) && span_fits(true) &&
+                  span_fits(false);
   int vec = v4 ? 4 : 1;
   auto tile = [&](int v) {
     g.nlow = 0;
@@ -476,8 +499,29 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
       r /= e;
     }
   }
+  // a vector width holds only if every group start is aligned to it: the
+  // base, the contracted strides and the stride steps between group starts
+  auto aligned_to = [&](int w, bool is_a) {
+    if (w < 2) return true;
+    const uintptr_t base = (uintptr_t)(is_a ? g.A : g.B);
+    if (base % (w * es)) return false;
+    const int64_t* io = is_a ? g.ia : g.ib;
+    if (w == 2 && io[2] % 2) return false;
+    int64_t pre = 1;
+    for (int j = 0; j < g.nout; ++j) {
+      const int64_t st = is_a ? g.out[j].sa : g.out[j].sb;
+      const int64_t step = pre >= vec ? 1 : vec / pre;  // digit step between group starts
+      if ((st * step) % w) return false;
+      pre *= g.out[j].div.d;
+    }
+    for (int j = 0; j < g.nk; ++j)
+      if ((is_a ? g.kmodes[j].sa : g.kmodes[j].sb) % w) return false;
+    return true;
+  };
   g.wa = width(g.ia);
   g.wb = width(g.ib);
+  if (!aligned_to(g.wa, true)) g.wa = 1;
+  if (!aligned_to(g.wb, false)) g.wb = 1;
   g.P = (int32_t)P;
   g.rows = g.total / P;
   if (g.rows >= (int64_t(1) << 32)) return set_error(OM_ERR_INVALID, "gemm_node: too many rows");
