@@ -419,10 +419,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-check", action="store_true")
-    ap.add_argument("--case", default="headline", choices=["headline", "config2", "contract", "network"],
+    ap.add_argument("--case", default="headline", choices=["headline", "config2", "contract", "network", "slices"],
                     help="profiling cases: config2 = only the config-2 permuted "
                          "contraction; contract = only warmup + steps headline calls; "
-                         "network = only the sliced MIS network, with its kernel breakdown")
+                         "network = only the sliced MIS network, with its kernel breakdown; "
+                         "slices = ten eager slice contractions of that network (profiling)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -450,6 +451,24 @@ def main():
         net["kernels_ms_total"] = {k: [round(v[0], 3), v[1]] for k, v in
                                    sorted(prof.items(), key=lambda kv: -kv[1][0])}
         print(json.dumps(net), flush=True)
+        be.close()
+        return
+    if args.case == "slices" and world == 1:
+        import importlib
+        import torch
+        om = load_pkg()
+        torch.cuda.set_device(local_rank)
+        be = om.B200(local_rank)
+        E = importlib.import_module("omeinsum_b200.einsum")
+        N = importlib.import_module("omeinsum_b200.network")
+        ixs, iy, sizes, ts, _ = E.mis_network(NET_N, SEED)
+        tree = E.elimination_tree(ixs, iy, sizes, E.min_fill_order(ixs, iy, 0, 8))
+        sliced = N.choose_slices(ixs, iy, sizes, tree, NET_SLICED, E.tree_cost)
+        ex = N.DeviceExecutor(be, E, "maxplus", ixs, iy, sizes, ts, tree, use_graph=False)
+        assigns = N.slice_assignments(sliced, sizes)
+        vals = [ex.value(assigns[q]) for q in range(10)]
+        print(json.dumps({"case": "slices", "values": vals}), flush=True)
+        del ex
         be.close()
         return
     if args.case == "contract":
