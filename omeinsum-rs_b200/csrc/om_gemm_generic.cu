@@ -226,7 +226,7 @@ __device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], 
 }
 
 template <typename T, int ALG, bool ARGMAX, int KT, int V>
-__global__ void __launch_bounds__(256) gemm_node(NodeArgs g) {
+__global__ void __launch_bounds__(256, 8) gemm_node(NodeArgs g) {
   using S = Semi<ALG, T>;
   // four-output groups run on 32-bit offsets (the launcher checks that
   // every offset of both operands fits); single outputs keep 64-bit ones
