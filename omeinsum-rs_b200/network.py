@@ -420,6 +420,54 @@ def scatter_slice_grad(grad_view, ix, sizes, assign, full_size):
     return full
 
 
+class SliceGradLayout:
+    """Where the gradient of every sliced view lands in the concatenation of
+    the full input tensors: one index array for all views, shifted per slice
+    by a per-view offset (vectorised scatter_slice_grad)."""
+
+    def __init__(self, ixs, sizes, sliced):
+        sl = set(sliced)
+        self.full_sizes = [int(np.prod([sizes[l] for l in ix])) for ix in ixs]
+        bases = np.cumsum([0] + self.full_sizes[:-1])
+        idx, view_of, self.fixed = [], [], []
+        for v, (ix, base) in enumerate(zip(ixs, bases)):
+            shape = [sizes[l] for l in ix]
+            st, acc = [], 1
+            for d in shape:
+                st.append(acc)
+                acc *= d
+            vs = [d for l, d in zip(ix, shape) if l not in sl]
+            vst = [t for l, t in zip(ix, st) if l not in sl]
+            i = np.zeros(max(1, int(np.prod(vs))), dtype=np.int64) + base
+            rem = np.arange(len(i))
+            for d, t in zip(vs, vst):
+                i += (rem % d) * t
+                rem //= d
+            idx.append(i)
+            view_of.append(np.full(len(i), v, dtype=np.int64))
+            self.fixed.append([(l, t) for l, t in zip(ix, st) if l in sl])
+        self.idx = np.concatenate(idx)
+        self.view_of = np.concatenate(view_of)
+        self.total = int(sum(self.full_sizes))
+
+    def scatter(self, grads, assign):
+        offs = np.array([sum(assign[l] * t for l, t in f) for f in self.fixed], dtype=np.int64)
+        out = np.zeros(self.total, dtype=np.float64)
+        out[self.idx + offs[self.view_of]] = np.concatenate(
+            [np.asarray(g, dtype=np.float64).reshape(-1) for g in grads])
+        return out
+
+
+_layouts = {}
+
+
+def _layout(ixs, sizes, sliced):
+    key = (id(ixs), tuple(sliced))
+    if key not in _layouts:
+        _layouts[key] = (ixs, SliceGradLayout(ixs, sizes, sliced))  # ixs kept alive with its id
+    return _layouts[key][1]
+
+
 def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device=None):
     """Contracts all 2^k slices over `world` ranks and combines them.
 
@@ -454,9 +502,7 @@ def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device
         if owner == rank:
             v, g = executor.value_and_grad(assigns[win])
             value[0] = v
-            parts = [scatter_slice_grad(gi, ix, sizes, assigns[win], n)
-                     for gi, ix, n in zip(g, ixs, full_sizes)]
-            grads = np.concatenate(parts).astype(np.float64)
+            grads = _layout(ixs, sizes, sliced).scatter(g, assigns[win])
         buf = torch.tensor(np.concatenate([value, grads]), dtype=torch.float64, device=device)
         if dist is not None and world > 1:
             dist.broadcast(buf, src=owner)
@@ -467,9 +513,8 @@ def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device
     total = np.zeros(1 + sum(full_sizes), dtype=np.float64)
     for s in mine:
         v, g = executor.value_and_grad(assigns[s])
-        parts = [scatter_slice_grad(gi, ix, sizes, assigns[s], n)
-                 for gi, ix, n in zip(g, ixs, full_sizes)]
-        total += np.concatenate([[v]] + parts)
+        total[0] += v
+        total[1:] += _layout(ixs, sizes, sliced).scatter(g, assigns[s])
     buf = torch.tensor(total, dtype=torch.float64, device=device)
     if dist is not None and world > 1:
         dist.all_reduce(buf, op=dist.ReduceOp.SUM)

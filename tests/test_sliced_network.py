@@ -95,3 +95,22 @@ def test_order_key_is_monotone():
     assert keys == sorted(keys)
     keys = [N.order_key(v, True) for v in vals]
     assert keys == sorted(keys, reverse=True)
+
+
+def test_slice_grad_layout_matches_scatter():
+    """The vectorised placement of sliced-view gradients equals the per-view
+    scatter_slice_grad for every slice."""
+    import importlib
+    load_pkg()
+    N = importlib.import_module("omeinsum_b200.network")
+    ixs = [[0, 1, 2], [2, 3], [1], [3, 0]]
+    sizes = {0: 2, 1: 3, 2: 2, 3: 4}
+    sl = [1, 3]
+    rng = np.random.default_rng(0)
+    lay = N.SliceGradLayout(ixs, sizes, sl)
+    for a in N.slice_assignments(sl, sizes):
+        g = [rng.normal(size=int(np.prod([sizes[l] for l in ix if l not in sl]))) for ix in ixs]
+        ref = np.concatenate([N.scatter_slice_grad(gi, ix, sizes, a,
+                                                   int(np.prod([sizes[l] for l in ix])))
+                              for gi, ix in zip(g, ixs)])
+        assert np.array_equal(ref, lay.scatter(g, a))
