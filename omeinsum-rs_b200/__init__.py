@@ -142,7 +142,7 @@ class Graph:
         _check(lib().om_b200_graph_launch(self.be.h, self.h))
 
     def __del__(self):
-        if getattr(self, "h", None) and lib is not None:
+        if getattr(self, "h", None):
             try:
                 lib().om_b200_graph_free(self.h)
             except Exception:

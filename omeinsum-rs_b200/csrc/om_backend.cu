@@ -348,6 +348,7 @@ struct om_graph {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   om::Arena* arena = nullptr;  // the recorded work's buffers
+  int device = 0;
 };
 
 extern "C" int om_b200_graph_begin(om_backend* be) {
@@ -389,7 +390,7 @@ extern "C" int om_b200_graph_end(om_backend* be, om_graph** graph_out) {
     drop_arena();
     return check_cuda(e, "cudaGraphInstantiate");
   }
-  *graph_out = new om_graph{g, x, arena};
+  *graph_out = new om_graph{g, x, arena, be->device};
   return OM_OK;
 }
 
@@ -406,6 +407,7 @@ extern "C" int om_b200_graph_free(om_graph* graph) {
   if (graph->exec) cudaGraphExecDestroy(graph->exec);
   if (graph->graph) cudaGraphDestroy(graph->graph);
   if (graph->arena) {
+    cudaSetDevice(graph->device);
     cudaDeviceSynchronize();  // a replay may still use the buffers
     om::arena_unregister(graph->arena);
     graph->arena->destroy();
