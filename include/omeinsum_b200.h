@@ -4,7 +4,7 @@
  *
  * The entry points replace the reference's `Backend` trait for a new `B200`
  * backend (tensor4all/omeinsum-rs, src/backend/traits.rs:42-199): a Rust
- * `impl Backend for B200` binds them one-to-one (see INTEGRATION.md).
+ * `impl Backend for B200` binds them one-to-one.
  *
  * Conventions (same as the reference):
  *   - tensors are column-major: axis 0 is fastest; strides count ELEMENTS;
@@ -123,6 +123,26 @@ int om_b200_tropical_backward(om_backend* be, om_dtype dtype,
                               int ndb, const int64_t* shape_b, const int32_t* modes_b,
                               int ndc, const int64_t* shape_c, const int32_t* modes_c,
                               void* grad_a, void* grad_b);
+
+/* Arithmetic of Standard<f32> products (no counterpart in the reference,
+ * whose faer path is plain f32):
+ *   OM_F32_TENSOR_3XTF32 (default): shapes of at least 64 x 64 x 16 run on the
+ *     tensor cores (tcgen05) as three TF32 products per f32 product
+ *     (A_lo B_hi + A_hi B_lo + A_hi B_hi) accumulated in f32; the error is
+ *     about 2^-21 * sum_k |a||b|.  Smaller shapes use the exact path.
+ *   OM_F32_EXACT: every Standard f32 product is an f32 FMA on the CUDA cores.
+ * The environment variable OM_DISABLE_TCGEN05 (any value) makes OM_F32_EXACT
+ * the default of new backends.  f64 and the tropical algebras are unaffected. */
+typedef enum { OM_F32_TENSOR_3XTF32 = 0, OM_F32_EXACT = 1 } om_f32_mode;
+int om_b200_set_f32_mode(om_backend* be, om_f32_mode mode);
+
+/* dst[idx[i]] = src[i] (accumulate == 0) or dst[idx[i]] += src[i]
+ * (accumulate != 0) for 0 <= i < n; idx is a device array of distinct int64
+ * element offsets into dst.  No counterpart in the reference: the sliced
+ * network driver uses it to place a slice's gradients (views of the inputs)
+ * into the full gradient tensors on the device, and to sum slices there. */
+int om_b200_scatter_index(om_backend* be, om_dtype dtype, const void* src, int64_t n,
+                          const int64_t* idx, void* dst, int accumulate);
 
 /* Kernel launches issued by this thread since the last call (counter reset
  * on read); used by benchmarks to report how many device kernels ran. */

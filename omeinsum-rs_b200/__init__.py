@@ -39,6 +39,7 @@ EXPORTS = [
     "om_b200_tropical_matmul_argmax_noalloc", "om_b200_einsum", "om_b200_einsum_backward",
     "om_b200_tape_free", "om_b200_graph_begin", "om_b200_graph_end", "om_b200_graph_launch",
     "om_b200_graph_free", "om_b200_tape_release", "om_b200_einsum_backward_linked",
+    "om_b200_set_f32_mode", "om_b200_scatter_index",
 ]
 
 
@@ -87,6 +88,8 @@ def lib():
         L.om_b200_graph_launch.argtypes = [P, P]
         L.om_b200_graph_free.argtypes = [P]
         L.om_b200_profile_enable.argtypes = [P, I]
+        L.om_b200_set_f32_mode.argtypes = [P, I]
+        L.om_b200_scatter_index.argtypes = [P, I, P, I64, P, P, I]
         L.om_b200_profile_query.argtypes = [P, I, ctypes.c_char_p, SZ,
                                             ctypes.POINTER(ctypes.c_double),
                                             ctypes.POINTER(ctypes.c_int64)]
@@ -241,6 +244,11 @@ class B200:
         g = ctypes.c_void_p()
         _check(lib().om_b200_graph_end(self.h, ctypes.byref(g)))
         return Graph(self, g.value)
+
+    def set_f32_mode(self, mode: str):
+        """'3xtf32' (tensor cores, default) or 'exact' (f32 FMA on the CUDA
+        cores) for Standard<f32> products."""
+        _check(lib().om_b200_set_f32_mode(self.h, {"3xtf32": 0, "exact": 1}[mode]))
 
     def profile(self, on: bool = True):
         """Turn per-kernel CUDA-event timing on (clearing it) or off."""

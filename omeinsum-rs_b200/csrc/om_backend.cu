@@ -252,6 +252,7 @@ int om_b200_create(int device, om_backend** out) {
     delete be;
     return check_cuda(e, "cudaMalloc(flags)");
   }
+  be->f32_exact = std::getenv("OM_DISABLE_TCGEN05") != nullptr;
   backend_live(be, true);
   *out = be;
   return OM_OK;
@@ -263,8 +264,22 @@ int om_b200_destroy(om_backend* be) {
   cudaSetDevice(be->device);
   resolve_pending(be);
   cudaFree(be->d_flags);
+  be->d_flags = nullptr;
   cudaStreamDestroy(be->stream);
-  delete be;
+  be->stream = nullptr;
+  be->pending.clear();
+  be->prof_totals.clear();
+  // The control block itself is kept (a few hundred bytes per destroyed
+  // backend): buffers released after om_b200_destroy are recognised by this
+  // address, and a later om_b200_create must never reuse it.
+  return OM_OK;
+}
+
+int om_b200_set_f32_mode(om_backend* be, om_f32_mode mode) {
+  if (!be) return set_error(OM_ERR_INVALID, "om_b200_set_f32_mode: null backend");
+  if (mode != OM_F32_TENSOR_3XTF32 && mode != OM_F32_EXACT)
+    return set_error(OM_ERR_INVALID, "om_b200_set_f32_mode: unknown mode");
+  be->f32_exact = mode == OM_F32_EXACT;
   return OM_OK;
 }
 
@@ -407,11 +422,14 @@ extern "C" int om_b200_graph_free(om_graph* graph) {
   if (graph->exec) cudaGraphExecDestroy(graph->exec);
   if (graph->graph) cudaGraphDestroy(graph->graph);
   if (graph->arena) {
+    int prev = -1;
+    cudaGetDevice(&prev);
     cudaSetDevice(graph->device);
     cudaDeviceSynchronize();  // a replay may still use the buffers
     om::arena_unregister(graph->arena);
     graph->arena->destroy();
     delete graph->arena;
+    if (prev >= 0) cudaSetDevice(prev);  // the caller's current device
   }
   delete graph;
   return OM_OK;

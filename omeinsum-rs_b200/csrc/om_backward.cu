@@ -136,3 +136,45 @@ extern "C" int om_b200_tropical_backward(om_backend* be, om_dtype dtype, const v
   note_launch();
   return check_cuda(cudaGetLastError(), "tropical_scatter launch");
 }
+
+// ---- index scatter -----------------------------------------------------------
+// dst[idx[i]] (+)= src[i]: places the gradient of a slice of a sliced network
+// (a strided view of each input tensor) into the full tensors' buffer, or sums
+// several slices' gradients there.  The indices are distinct within one call,
+// so no atomics are needed.
+namespace om {
+namespace {
+template <typename T>
+__global__ void scatter_index_kernel(const T* __restrict__ src, const int64_t* __restrict__ idx,
+                                     T* __restrict__ dst, int64_t n, int accumulate) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = idx[i];
+    dst[j] = accumulate ? dst[j] + src[i] : src[i];
+  }
+}
+}  // namespace
+}  // namespace om
+
+extern "C" int om_b200_scatter_index(om_backend* be, om_dtype dtype, const void* src, int64_t n,
+                                     const int64_t* idx, void* dst, int accumulate) {
+  using namespace om;
+  if (!be || (n > 0 && (!src || !idx || !dst)))
+    return set_error(OM_ERR_INVALID, "om_b200_scatter_index: null argument");
+  if (n < 0) return set_error(OM_ERR_INVALID, "om_b200_scatter_index: negative length");
+  if (n == 0) return OM_OK;
+  OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  const int blocks =
+      (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)be->num_sms * 8));
+  ProfScope prof(be, "scatter_index");
+  if (dtype == OM_F32)
+    scatter_index_kernel<float><<<blocks, 256, 0, be->stream>>>((const float*)src, idx,
+                                                                (float*)dst, n, accumulate);
+  else if (dtype == OM_F64)
+    scatter_index_kernel<double><<<blocks, 256, 0, be->stream>>>((const double*)src, idx,
+                                                                 (double*)dst, n, accumulate);
+  else
+    return set_error(OM_ERR_UNSUPPORTED, "om_b200_scatter_index: dtype must be f32 or f64");
+  note_launch();
+  return check_cuda(cudaGetLastError(), "scatter_index launch");
+}

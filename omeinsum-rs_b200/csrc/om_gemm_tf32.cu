@@ -348,8 +348,7 @@ int launch_gemm_tf32(om_backend* be, const GemmArgs& g, bool* handled) {
   if (g.dtype != OM_F32 || g.alg != OM_STANDARD || g.argmax) return OM_OK;
   if (g.M < 64 || g.N < 64 || g.K < 16 || g.batch > 65535) return OM_OK;
   if (g.M > (1 << 30) || g.N > (1 << 30) || g.K > (1 << 30)) return OM_OK;
-  static const bool disabled = getenv("OM_DISABLE_TCGEN05") != nullptr;
-  if (disabled) return OM_OK;
+  if (be->f32_exact) return OM_OK;
   const int64_t Kp = (g.K + TK - 1) / TK * TK;
   const size_t na = (size_t)(g.batch * g.M * Kp), nb = (size_t)(g.batch * g.N * Kp);
   Scratch ws;

@@ -26,6 +26,8 @@ struct om_backend {
   // device flag word used by kernels that pick a path on the device
   // (special-value scan of the fast tropical GEMM); lives for the backend.
   uint32_t* d_flags = nullptr;
+  // Standard f32 products on the tensor cores (3xTF32) or exact FMA
+  bool f32_exact = false;
   // per-kernel event timing (om_b200_profile_*)
   bool profiling = false;
   struct Pending {

@@ -278,8 +278,9 @@ class DeviceExecutor:
         plan = self._ensure_plan(assign)
         ein = plan["ein"]
         out = self.be.alloc(ein.out_size(), self.dtype)
-        # every gradient the call returns lives in one buffer, read back once:
-        # the reduced tree's leaves, then each hoisted subtree's leaves
+        # every gradient lives in one buffer: first the input tensors' (the
+        # reduced tree's plain leaves, then each hoisted subtree's leaves --
+        # the order of _gbuf_order), then the hoisted intermediates' own
         leaves = self._reduce(key)[0]
         om = sys.modules[type(self.be).__module__]
         sizes_red = [max(1, int(np.prod(v[1]))) for v in plan["views"]]
@@ -287,18 +288,24 @@ class DeviceExecutor:
                      if lf[0] == "hoisted" else [] for lf in leaves]
         total = sum(sizes_red) + sum(sum(x) for x in sub_sizes)
         gbuf = self.be.alloc(total, self.dtype)
-        at, grads, sub_grads = 0, [], []
-        for n in sizes_red:
-            grads.append(om.View(gbuf, at, n))
-            at += n
+        at, grads, sub_grads = 0, [None] * len(leaves), []
+        for j, (lf, n) in enumerate(zip(leaves, sizes_red)):
+            if lf[0] == "leaf":
+                grads[j] = om.View(gbuf, at, n)
+                at += n
         for sz in sub_sizes:
             row = []
             for n in sz:
                 row.append(om.View(gbuf, at, n))
                 at += n
             sub_grads.append(row)
+        inputs_end = at
+        for j, (lf, n) in enumerate(zip(leaves, sizes_red)):
+            if lf[0] == "hoisted":
+                grads[j] = om.View(gbuf, at, n)
+                at += n
         gp = {"ein": ein, "out": out, "grads": grads, "sub_grads": sub_grads, "gbuf": gbuf,
-              "graph": None, "tape": None, "plan": plan}
+              "inputs_end": inputs_end, "graph": None, "tape": None, "plan": plan}
         if self.use_graph:
             self._stage(plan, assign)
             self.be.graph_begin()
@@ -312,7 +319,10 @@ class DeviceExecutor:
         self._grad_plans[key] = gp
         return gp
 
-    def value_and_grad(self, assign, dy=1.0):
+    def _grad_device(self, assign, dy=1.0):
+        """Runs the slice's forward with tape and its backward; the gradients
+        stay in the plan's device buffer (gp["gbuf"]) and the value in
+        gp["out"].  Returns the gradient plan."""
         gp = self._grad_plan(assign)
         plan = gp["plan"]
         self._stage(plan, assign)
@@ -325,13 +335,18 @@ class DeviceExecutor:
         leaves = self._reduce(assign.keys())[0]
         links = [(j, lf[3], sg) for j, (lf, sg) in enumerate(zip(leaves, gp["sub_grads"]))
                  if lf[0] == "hoisted"]
+        if "dy" not in gp:
+            gp["dy"] = self.be.alloc(1, self.dtype)
+            gp["dy_val"] = None
+        if gp["dy_val"] != dy:
+            self.be.upload_into(gp["dy"], np.asarray([dy], self.dtype))
+            gp["dy_val"] = dy
         try:
-            d = self.be.from_slice(np.asarray([dy], self.dtype))
             try:  # one launch through the reduced tape and the hoisted ones
-                self.E.Einsum.backward_tape_linked(tape, d, gp["grads"], links)
+                self.E.Einsum.backward_tape_linked(tape, gp["dy"], gp["grads"], links)
                 links = []
             except sys.modules[type(self.be).__module__].OmError:
-                gp["ein"].backward_tape(tape, d, gp["grads"])
+                gp["ein"].backward_tape(tape, gp["dy"], gp["grads"])
         finally:
             if gp["graph"] is None:
                 gp["ein"].tape_free(tape)
@@ -339,19 +354,55 @@ class DeviceExecutor:
                 gp["ein"].tape_release(tape)
         for j, sub_tape, sg in links:  # on through each hoisted subtree's tape
             self.E.Einsum.backward_tape(sub_tape, gp["grads"][j], sg)
+        return gp
+
+    def _gbuf_order(self, key):
+        """Input tensor of each region of the gradient buffer, in buffer order
+        (the reduced tree's leaves, then each hoisted subtree's leaves)."""
+        leaves = self._reduce(key)[0]
+        order = [lf[1] for lf in leaves if lf[0] == "leaf"]
+        for lf in leaves:
+            if lf[0] == "hoisted":
+                order.extend(lf[4])
+        return order
+
+    def value_and_grad(self, assign, dy=1.0):
+        gp = self._grad_device(assign, dy)
         host = gp["gbuf"].to_vec()
         out = [None] * len(self.ixs)
-        base = gp["gbuf"].ptr
-        es = np.dtype(self.dtype).itemsize
-        for lf, g, sg in zip(leaves, gp["grads"], gp["sub_grads"]):
-            if lf[0] == "leaf":
-                o = (g.ptr - base) // es
-                out[lf[1]] = host[o:o + g.n].copy()
-            else:
-                for i, v in zip(lf[4], sg):
-                    o = (v.ptr - base) // es
-                    out[i] = host[o:o + v.n].copy()
+        at = 0
+        for i in self._gbuf_order(frozenset(assign.keys())):
+            n = max(1, int(np.prod([self.sizes[l] for l in self.ixs[i] if l not in assign])))
+            out[i] = host[at:at + n].copy()
+            at += n
         return float(gp["out"].to_vec()[0]), out
+
+    def place_index(self, layout, assign):
+        """Device int64 array: for every element of the gradient buffer, its
+        position in the concatenation of the full input tensors, shifted by
+        one (position 0 is the value).  Cached per slice."""
+        cache = self.__dict__.setdefault("_place", {})
+        key = tuple(sorted(assign.items()))
+        if key not in cache:
+            idx = 1 + layout.index_for(self._gbuf_order(frozenset(assign.keys())), assign)
+            cache[key] = self.be.from_slice(idx.astype(np.int64))
+        return cache[key]
+
+    def grad_into(self, assign, layout, dst_ptr, accumulate, dy=1.0):
+        """Runs the slice's gradient and places value and gradients into the
+        device buffer at dst_ptr ([value, full gradients...], the executor's
+        dtype): written, or added when `accumulate`.  Nothing is read back."""
+        gp = self._grad_device(assign, dy)
+        om = sys.modules[type(self.be).__module__]
+        L = om.lib()
+        dt = om.DTYPES[np.dtype(self.dtype)]
+        idx = self.place_index(layout, assign)
+        om._check(L.om_b200_scatter_index(self.be.h, dt, gp["gbuf"].ptr, len(idx), idx.ptr,
+                                          dst_ptr, 1 if accumulate else 0))
+        if "zero_idx" not in self.__dict__:
+            self.zero_idx = self.be.from_slice(np.zeros(1, np.int64))
+        om._check(L.om_b200_scatter_index(self.be.h, dt, gp["out"].ptr, 1, self.zero_idx.ptr,
+                                          dst_ptr, 1 if accumulate else 0))
 
     def __del__(self):
         for gp in getattr(self, "_grad_plans", {}).values():
@@ -448,7 +499,14 @@ class SliceGradLayout:
             self.fixed.append([(l, t) for l, t in zip(ix, st) if l in sl])
         self.idx = np.concatenate(idx)
         self.view_of = np.concatenate(view_of)
+        self.per_view = idx
         self.total = int(sum(self.full_sizes))
+
+    def index_for(self, order, assign):
+        """Positions in the full buffer of the views' elements when the views
+        are concatenated in `order` (input tensor indices) for this slice."""
+        return np.concatenate([self.per_view[v] + sum(assign[l] * t for l, t in self.fixed[v])
+                               for v in order])
 
     def scatter(self, grads, assign):
         offs = np.array([sum(assign[l] * t for l, t in f) for f in self.fixed], dtype=np.int64)
@@ -462,24 +520,76 @@ _layouts = {}
 
 
 def _layout(ixs, sizes, sliced):
-    key = (id(ixs), tuple(sliced))
-    if key not in _layouts:
-        _layouts[key] = (ixs, SliceGradLayout(ixs, sizes, sliced))  # ixs kept alive with its id
-    return _layouts[key][1]
+    """SliceGradLayout of (ixs, sizes, sliced), cached by value (a few recent
+    networks)."""
+    key = (tuple(tuple(ix) for ix in ixs), tuple(sorted(sizes.items())), tuple(sliced))
+    lay = _layouts.get(key)
+    if lay is None:
+        if len(_layouts) >= 8:
+            _layouts.pop(next(iter(_layouts)))
+        lay = _layouts[key] = SliceGradLayout(ixs, sizes, sliced)
+    return lay
 
 
-def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device=None):
+# algebra -> minimise?  (the tropical combine keeps the best slice)
+TROPICAL = {"maxplus": False, "minplus": True, "maxmul": False}
+
+
+class CombineError(RuntimeError):
+    """A collective of the combine step failed or ran past its time limit
+    (a rank that left, a lost connection).  The reference has no multi-GPU
+    path; like its other failures this is reported, not hung on."""
+
+
+def _collective(dist, op, timeout_s, what):
+    """Runs `op(async_op=True)` and waits at most timeout_s for it."""
+    import datetime
+    try:
+        work = op(async_op=True)
+        if not work.wait(timeout=datetime.timedelta(seconds=timeout_s)):
+            raise CombineError(f"{what}: not completed within {timeout_s} s")
+    except CombineError:
+        raise
+    except Exception as e:  # gloo / NCCL report a lost peer or a timeout
+        raise CombineError(f"{what} failed: {e}") from e
+
+
+def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device=None,
+               timeout_s=120.0):
     """Contracts all 2^k slices over `world` ranks and combines them.
 
     Returns (value, gradients of every input tensor, winning slice id or -1).
     `dist` is torch.distributed (None for a single process); collectives run
-    on `device` tensors (CUDA for NCCL, CPU for gloo)."""
+    on `device` tensors (CUDA for NCCL, CPU for gloo) and each waits at most
+    `timeout_s` seconds, after which CombineError is raised.
+
+    With a DeviceExecutor everything stays on the device until one read-back
+    of the combined buffer: slice gradients are placed into the full tensors
+    by om_b200_scatter_index, the collectives run on that buffer on the
+    backend's stream, and only the tropical slice values (one per slice) and
+    the winning key come back to the host before it."""
     import torch
+    if alg not in TROPICAL and alg != "standard":
+        raise ValueError(f"run_sliced: unknown algebra {alg!r}")
     assigns = slice_assignments(sliced, sizes)
     mine = [s for s in range(len(assigns)) if s % world == rank]
     full_sizes = [int(np.prod([sizes[l] for l in ix])) for ix in ixs]
-    if alg in ("maxplus", "minplus"):
-        minimize = alg == "minplus"
+    layout = _layout(ixs, sizes, sliced)
+    multi = dist is not None and world > 1
+    on_device = isinstance(executor, DeviceExecutor)
+    if on_device:
+        if device is None:
+            device = torch.device(f"cuda:{executor.be.device}")
+        stream = torch.cuda.ExternalStream(executor.be.stream(), device=device)
+        tdt = torch.float64 if executor.dtype == np.float64 else torch.float32
+    import contextlib
+    ctx = torch.cuda.stream(stream) if on_device else contextlib.nullcontext()
+
+    def split(out):
+        return np.split(out[1:], np.cumsum(full_sizes)[:-1])
+
+    if alg in TROPICAL:
+        minimize = TROPICAL[alg]
         best = None
         if hasattr(executor, "values"):
             vals = executor.values([assigns[s] for s in mine])
@@ -491,32 +601,56 @@ def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device
                 best = key
         # int64 MAX on the unsigned key: shift it into signed order first
         signed = (best - (1 << 63)) if best is not None else -(1 << 63)
-        key = torch.tensor([signed], dtype=torch.int64, device=device)
-        if dist is not None and world > 1:
-            dist.all_reduce(key, op=dist.ReduceOp.MAX)
+        with ctx:
+            key = torch.tensor([signed], dtype=torch.int64, device=device)
+        if multi:
+            with ctx:
+                _collective(dist, lambda **kw: dist.all_reduce(key, op=dist.ReduceOp.MAX, **kw),
+                            timeout_s, "slice-key all-reduce")
         k = int(key.item()) + (1 << 63)
         win = 0xFFFFFFFF - (k & 0xFFFFFFFF)
         owner = win % world
-        grads = np.zeros(sum(full_sizes), dtype=np.float64)
+        if on_device:
+            with ctx:  # every device step on the backend's stream
+                buf = torch.zeros(1 + layout.total, dtype=tdt, device=device)
+                if owner == rank:
+                    executor.grad_into(assigns[win], layout, buf.data_ptr(), accumulate=False)
+                if multi:
+                    _collective(dist, lambda **kw: dist.broadcast(buf, src=owner, **kw),
+                                timeout_s, "gradient broadcast")
+                out = buf.cpu().numpy()
+            return float(out[0]), split(out), win
+        grads = np.zeros(layout.total, dtype=np.float64)
         value = np.zeros(1)
         if owner == rank:
             v, g = executor.value_and_grad(assigns[win])
             value[0] = v
-            grads = _layout(ixs, sizes, sliced).scatter(g, assigns[win])
+            grads = layout.scatter(g, assigns[win])
         buf = torch.tensor(np.concatenate([value, grads]), dtype=torch.float64, device=device)
-        if dist is not None and world > 1:
-            dist.broadcast(buf, src=owner)
+        if multi:
+            _collective(dist, lambda **kw: dist.broadcast(buf, src=owner, **kw), timeout_s,
+                        "gradient broadcast")
         out = buf.cpu().numpy()
-        g = np.split(out[1:], np.cumsum(full_sizes)[:-1])
-        return float(out[0]), g, win
+        return float(out[0]), split(out), win
     # Standard: sum of slices
-    total = np.zeros(1 + sum(full_sizes), dtype=np.float64)
+    if on_device:
+        with ctx:
+            buf = torch.zeros(1 + layout.total, dtype=tdt, device=device)
+            for s in mine:
+                executor.grad_into(assigns[s], layout, buf.data_ptr(), accumulate=True)
+            if multi:
+                _collective(dist, lambda **kw: dist.all_reduce(buf, op=dist.ReduceOp.SUM, **kw),
+                            timeout_s, "slice-sum all-reduce")
+            out = buf.cpu().numpy()
+        return float(out[0]), split(out), -1
+    total = np.zeros(1 + layout.total, dtype=np.float64)
     for s in mine:
         v, g = executor.value_and_grad(assigns[s])
         total[0] += v
-        total[1:] += _layout(ixs, sizes, sliced).scatter(g, assigns[s])
+        total[1:] += layout.scatter(g, assigns[s])
     buf = torch.tensor(total, dtype=torch.float64, device=device)
-    if dist is not None and world > 1:
-        dist.all_reduce(buf, op=dist.ReduceOp.SUM)
+    if multi:
+        _collective(dist, lambda **kw: dist.all_reduce(buf, op=dist.ReduceOp.SUM, **kw),
+                    timeout_s, "slice-sum all-reduce")
     out = buf.cpu().numpy()
-    return float(out[0]), np.split(out[1:], np.cumsum(full_sizes)[:-1]), -1
+    return float(out[0]), split(out), -1

@@ -38,7 +38,7 @@ def run_oracle(k):
 
 
 def check_kat(k, c, am):
-    """Shared by the oracle test here and the device test (test_gpu_parity.py)."""
+    """Shared by the oracle test here and the device test (test_gpu_contract.py::test_reference_kat_on_device)."""
     dt = np.float32 if k["dtype"] == "f32" else np.float64
     n = int(np.prod(k["shape_c"])) if k["kind"] == "contract" and k["shape_c"] else None
     if k["kind"] == "contract":

@@ -25,6 +25,13 @@ def _case(kind):
     if kind == "mis":
         ixs, iy, sizes, ts, edges = E.mis_network(16, 9)
         alg = "maxplus"
+    elif kind == "maxmul":
+        # the same independent-set network in (max, x): vertex weights [1, 2],
+        # forbidden edge state 0, so the value is 2^|MIS|
+        ixs, iy, sizes, ts, edges = E.mis_network(16, 9)
+        ts = [np.array([1.0, 2.0], np.float32)] * 16 + \
+             [np.array([1.0, 1.0, 1.0, 0.0], np.float32)] * len(edges)
+        alg = "maxmul"
     else:
         ixs, iy, sizes, ts, edges = E.ising_network(14, 9)
         alg = "standard"
@@ -57,7 +64,7 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("kind", ["mis", "ising"])
+@pytest.mark.parametrize("kind", ["mis", "maxmul", "ising"])
 def test_two_gloo_ranks_match_single_rank_and_unsliced(kind):
     E, N, oe, alg, ixs, iy, sizes, ts, edges, tree, sliced = _case(kind)
     ctx = mp.get_context("spawn")
@@ -76,12 +83,13 @@ def test_two_gloo_ranks_match_single_rank_and_unsliced(kind):
     ch, niy = E.encode_tree(tree, ixs, iy)
     unsliced = oe.einsum(alg, ts, ixs, iy, sizes, ch, niy)[0]
     for rank, v, g, win in res:
-        if kind == "mis":
+        if kind in ("mis", "maxmul"):
             assert v == v1 == unsliced and win == w1
             for x, y in zip(g, g1):
                 np.testing.assert_array_equal(x, y)
-            sel = [int(np.asarray(x)[1] > np.asarray(x)[0]) for x in g[:16]]
-            assert sum(sel) == int(v) and all(not (sel[a] and sel[b]) for a, b in edges)
+            sel = [int(np.asarray(x)[1] != 0) for x in g[:16]]
+            size = int(v) if kind == "mis" else int(round(np.log2(v)))
+            assert sum(sel) == size and all(not (sel[a] and sel[b]) for a, b in edges)
         else:
             assert abs(v - unsliced) <= 1e-12 * abs(unsliced)
             for x, y in zip(g, g1):
@@ -114,3 +122,47 @@ def test_slice_grad_layout_matches_scatter():
                                                    int(np.prod([sizes[l] for l in ix])))
                               for gi, ix in zip(g, ixs)])
         assert np.array_equal(ref, lay.scatter(g, a))
+        # device placement index: views concatenated in any order
+        order = list(rng.permutation(len(ixs)))
+        full = np.zeros(lay.total)
+        full[lay.index_for(order, a)] = np.concatenate([g[v] for v in order])
+        assert np.array_equal(full, ref)
+
+
+def _leaving_worker(rank, world, port, q):
+    """Rank 1 computes its slices and leaves before the combine; rank 0 must
+    get CombineError within the collective's time limit instead of hanging."""
+    import sys
+    import time
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    E, N, oe, alg, ixs, iy, sizes, ts, edges, tree, sliced = _case("mis")
+    ex = N.OracleExecutor(oe, E, alg, ixs, iy, sizes, ts, tree)
+    if rank == 1:
+        ex.value(N.slice_assignments(sliced, sizes)[1])
+        os._exit(0)  # leaves between slices: no collective of its own in flight
+    t0 = time.time()
+    try:
+        N.run_sliced(ex, alg, ixs, sizes, sliced, rank, world, dist=dist, timeout_s=5.0)
+        q.put(("no error", time.time() - t0))
+    except N.CombineError as e:
+        q.put(("CombineError", time.time() - t0, str(e)[:200]))
+    os._exit(0)
+
+
+def test_rank_leaving_between_slices_gives_combine_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == "CombineError", res
+    assert res[1] < 60, res
