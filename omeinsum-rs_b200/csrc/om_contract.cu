@@ -95,6 +95,23 @@ int64_t group_size(const Operand& op, const std::vector<int32_t>& g) {
   return s;
 }
 
+// A group that does not flatten in `op` but splits into two flattening runs
+// (an inner run of k1 elements at stride s1, then the rest at stride s2),
+// with k1 a multiple of 32 (a 32-wide k tile never straddles the two runs).
+bool two_level(const Operand& op, const std::vector<int32_t>& g, int64_t& k1, int64_t& s1,
+               int64_t& s2) {
+  for (size_t p = g.size() - 1; p >= 1; --p) {
+    std::vector<int32_t> in(g.begin(), g.begin() + p), out(g.begin() + p, g.end());
+    const int64_t a = flat_stride(op, in), b = flat_stride(op, out);
+    if (a < 0 || b < 0) continue;
+    k1 = group_size(op, in);
+    s1 = a;
+    s2 = b;
+    return k1 % 32 == 0;
+  }
+  return false;
+}
+
 std::vector<int64_t> contiguous_strides(const std::vector<int64_t>& shape) {
   std::vector<int64_t> st(shape.size());
   int64_t s = 1;
@@ -393,14 +410,76 @@ int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Op
     }
   }
 
+  // Standard f32 on the tensor cores: the split pre-pass reads its operands
+  // through their strides anyway, so a group (free or contracted) that does
+  // not flatten in an operand but splits into two flattening runs is decoded
+  // there instead of gathered.  Group orders are chosen so that C is written
+  // directly and every two-level operand is still read along a unit-stride
+  // axis (its free group's or its contracted group's inner run).
+  struct Lv {
+    int64_t n1 = 0, s1 = 0, s2 = 0;  // n1 == 0: flat (stride s1)
+  };
+  Lv a_row, a_k, b_row, b_k;
+  bool decoded = false;
+  auto level = [&](const Operand& X, const std::vector<int32_t>& g, Lv& lv) {
+    lv = Lv{};
+    const int64_t f = flat_stride(X, g);
+    if (f >= 0) {
+      lv.s1 = f;
+      return true;
+    }
+    return g.size() >= 2 && two_level(X, g, lv.n1, lv.s1, lv.s2);
+  };
+  if (!track) {
+    const bool need = flat_stride(A, lfree) < 0 || flat_stride(A, contr) < 0 ||
+                      flat_stride(B, rfree) < 0 || flat_stride(B, contr) < 0 ||
+                      flat_stride(C, lfree) < 0 || flat_stride(C, rfree) < 0;
+    if (need && flat_stride(A, batch) >= 0 && flat_stride(B, batch) >= 0 &&
+        flat_stride(C, batch) >= 0 &&
+        tf32_takes(be, alg, dt, false, group_size(A, lfree), group_size(B, rfree),
+                   group_size(A, contr), group_size(A, batch))) {
+      const std::vector<std::vector<int32_t>> lc{lfree, sorted_by_stride(C, lfree),
+                                                 sorted_by_stride(A, lfree)};
+      const std::vector<std::vector<int32_t>> rc{rfree, sorted_by_stride(C, rfree),
+                                                 sorted_by_stride(B, rfree)};
+      const std::vector<std::vector<int32_t>> kc{contr, sorted_by_stride(A, contr),
+                                                 sorted_by_stride(B, contr)};
+      for (size_t i = 0; i < lc.size() && !decoded; ++i)
+        for (size_t j = 0; j < rc.size() && !decoded; ++j)
+          for (size_t k = 0; k < kc.size() && !decoded; ++k) {
+            if (flat_stride(C, lc[i]) < 0 || flat_stride(C, rc[j]) < 0) continue;
+            Lv ar, ak, br, bk;
+            if (!level(A, lc[i], ar) || !level(A, kc[k], ak) || !level(B, rc[j], br) ||
+                !level(B, kc[k], bk))
+              continue;
+            if (!(ar.s1 == 1 || ak.s1 == 1) || !(br.s1 == 1 || bk.s1 == 1)) continue;
+            lfree = lc[i];
+            rfree = rc[j];
+            contr = kc[k];
+            a_row = ar;
+            a_k = ak;
+            b_row = br;
+            b_k = bk;
+            decoded = true;
+            if (trace_on())
+              fprintf(stderr,
+                      "[om trace] tf32 split decodes two levels: A rows %lld k %lld, B cols %lld "
+                      "k %lld\n",
+                      (long long)ar.n1, (long long)ak.n1, (long long)br.n1, (long long)bk.n1);
+          }
+    }
+  }
+
   Scratch ga, gb;
-  if (flat_stride(A, lfree) < 0 || flat_stride(A, contr) < 0 || flat_stride(A, batch) < 0) {
+  if (!decoded &&
+      (flat_stride(A, lfree) < 0 || flat_stride(A, contr) < 0 || flat_stride(A, batch) < 0)) {
     Operand g;
     OM_TRY(gather_operand(be, es, a, A, lfree, contr, batch, ga, g));
     a = ga.ptr;
     A = g;
   }
-  if (flat_stride(B, contr) < 0 || flat_stride(B, rfree) < 0 || flat_stride(B, batch) < 0) {
+  if (!decoded &&
+      (flat_stride(B, contr) < 0 || flat_stride(B, rfree) < 0 || flat_stride(B, batch) < 0)) {
     Operand g;
     OM_TRY(gather_operand(be, es, b, B, contr, rfree, batch, gb, g));
     b = gb.ptr;
@@ -415,13 +494,23 @@ int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Op
   g.N = group_size(B, rfree);
   g.batch = group_size(A, batch);
   g.A = a;
-  g.sam = flat_stride(A, lfree);
-  g.sak = flat_stride(A, contr);
+  g.sam = decoded ? a_row.s1 : flat_stride(A, lfree);
+  g.sak = decoded ? a_k.s1 : flat_stride(A, contr);
   g.sab = flat_stride(A, batch);
   g.B = b;
-  g.sbk = flat_stride(B, contr);
-  g.sbn = flat_stride(B, rfree);
+  g.sbk = decoded ? b_k.s1 : flat_stride(B, contr);
+  g.sbn = decoded ? b_row.s1 : flat_stride(B, rfree);
   g.sbb = flat_stride(B, batch);
+  if (decoded) {
+    g.ka1 = a_k.n1;
+    g.sak2 = a_k.s2;
+    g.kb1 = b_k.n1;
+    g.sbk2 = b_k.s2;
+    g.ma1 = a_row.n1;
+    g.sam2 = a_row.s2;
+    g.nb1 = b_row.n1;
+    g.sbn2 = b_row.s2;
+  }
 
   const bool c_direct =
       flat_stride(C, lfree) >= 0 && flat_stride(C, rfree) >= 0 && flat_stride(C, batch) >= 0;

@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
 #include "om_internal.h"
@@ -104,6 +105,85 @@ __global__ void gather_transpose(const T* __restrict__ src, T* __restrict__ dst,
     for (int r = threadIdx.y; r < kTile; r += blockDim.y) {
       int64_t j = j0 + r, i = i0 + threadIdx.x;
       if (i < s0 && j < sp) dst[doff + i + j * dstride_p] = tile[threadIdx.x][r];
+    }
+  }
+}
+
+// Batched 32 x 32 transpose with 16-byte accesses on both sides: destination
+// axis 0 (unit stride in dst) against axis p (unit stride in src), both
+// multiples of 32, every other axis indexing tiles.  Each thread moves one
+// 16-byte vector per tile in and out of a padded shared tile (conflict-free
+// in both phases); a CTA takes kTv tiles per round so that several loads are
+// in flight per thread.
+constexpr int kTv = 2;
+
+template <typename T>
+__global__ void __launch_bounds__(256) gather_transpose_vec(const T* __restrict__ src,
+                                                            T* __restrict__ dst, GatherDesc d,
+                                                            int p, int64_t dstride_p,
+                                                            int64_t tiles0, int64_t tilesp,
+                                                            int64_t total_tiles) {
+  constexpr int V = 16 / sizeof(T);      // elements per vector
+  constexpr int VR = kTile / V;          // vectors per 32-element row
+  constexpr int UPT = kTile * VR / 256;  // vectors per thread per tile (1 or 2)
+  using Vec = typename std::conditional<sizeof(T) == 4, uint4, ulonglong2>::type;
+  __shared__ T tile[kTv][kTile][kTile + 1];
+  const int tid = threadIdx.x;
+  for (int64_t t0 = (int64_t)blockIdx.x * kTv; t0 < total_tiles; t0 += (int64_t)gridDim.x * kTv) {
+    int64_t soff[kTv], doff[kTv];
+    Vec v[kTv][UPT];
+#pragma unroll
+    for (int q = 0; q < kTv; ++q) {
+      const int64_t t = t0 + q;
+      soff[q] = doff[q] = -1;
+      if (t >= total_tiles) continue;
+      const int64_t ti = t % tiles0, rest = t / tiles0;
+      const int64_t tp = rest % tilesp;
+      int64_t rem = rest / tilesp, so = 0, dof = 0, dstr = d.shape[0];
+      for (int k = 1; k < d.nd; ++k) {
+        if (k == p) {
+          dstr *= d.shape[k];
+          continue;
+        }
+        const int64_t c = rem % d.shape[k];
+        rem /= d.shape[k];
+        so += c * d.sstride[k];
+        dof += c * dstr;
+        dstr *= d.shape[k];
+      }
+      soff[q] = so + ti * kTile * d.sstride[0] + tp * kTile;
+      doff[q] = dof + ti * kTile + tp * kTile * dstride_p;
+#pragma unroll
+      for (int u = 0; u < UPT; ++u) {
+        const int w = tid + 256 * u, i = w / VR, jv = w % VR;
+        v[q][u] = *(const Vec*)(src + soff[q] + i * d.sstride[0] + jv * V);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < kTv; ++q) {
+      if (soff[q] < 0) continue;
+#pragma unroll
+      for (int u = 0; u < UPT; ++u) {
+        const int w = tid + 256 * u, i = w / VR, jv = w % VR;
+        const T* e = (const T*)&v[q][u];
+#pragma unroll
+        for (int c = 0; c < V; ++c) tile[q][i][jv * V + c] = e[c];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < kTv; ++q) {
+      if (doff[q] < 0) continue;
+#pragma unroll
+      for (int u = 0; u < UPT; ++u) {
+        const int w = tid + 256 * u, j = w / VR, iv = w % VR;
+        Vec o;
+        T* e = (T*)&o;
+#pragma unroll
+        for (int c = 0; c < V; ++c) e[c] = tile[q][iv * V + c][j];
+        *(Vec*)(dst + doff[q] + iv * V + j * dstride_p) = o;
+      }
     }
   }
 }
@@ -342,6 +422,26 @@ int gather_typed(om_backend* be, const T* src, T* dst, GatherDesc d, int64_t n) 
     gather_rows<T><<<grid_for(be, rows, 1), threads, 0, be->stream>>>(src, dst, d, rows);
     note_launch();
     return check_cuda(cudaGetLastError(), "gather_rows launch");
+  }
+  {
+    // batched 32 x 32 transpose with 16-byte vectors on both sides
+    int pv = -1;
+    for (int k = 1; k < d.nd; ++k)
+      if (d.sstride[k] == 1) pv = k;
+    constexpr int64_t V = 16 / sizeof(T);
+    bool vec = pv > 0 && d.shape[0] % kTile == 0 && d.shape[pv] % kTile == 0 &&
+               ((uintptr_t)src % 16) == 0 && ((uintptr_t)dst % 16) == 0;
+    for (int k = 0; k < d.nd && vec; ++k)
+      if (k != pv && d.sstride[k] % V != 0) vec = false;
+    if (vec) {
+      const int64_t tiles0 = d.shape[0] / kTile, tilesp = d.shape[pv] / kTile;
+      const int64_t total = n / (kTile * kTile);
+      const int64_t g = std::min<int64_t>((total + kTv - 1) / kTv, (int64_t)be->num_sms * 8);
+      gather_transpose_vec<T><<<(int)std::max<int64_t>(g, 1), 256, 0, be->stream>>>(
+          src, dst, d, pv, dstr[pv], tiles0, tilesp, total);
+      note_launch();
+      return check_cuda(cudaGetLastError(), "gather_transpose_vec launch");
+    }
   }
   {
     PermDesc pd;

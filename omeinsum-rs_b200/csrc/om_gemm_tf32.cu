@@ -5,8 +5,8 @@
 // Every f32 operand x is split into hi = tf32(x) (round to nearest) and
 // lo = tf32(x - hi); the product is accumulated as
 //     A_lo B_hi + A_hi B_lo + A_hi B_hi
-// in f32 in tensor memory, which keeps the error near f32 rounding
-// (|error| ~ 2^-21 * sum_k |a||b|, inside the 1e-5 tolerance of the tests).
+// in f32, chunk by chunk in tensor memory and across chunks in registers
+// (see CHUNK), which keeps the error near that of an f32 FMA loop.
 //
 // Two kernels:
 //   split_tf32_kernel  one HBM pass: reads an operand through its strides
@@ -16,16 +16,21 @@
 //                      with the split, staged through a 32 x 32 shared tile so
 //                      reads and writes stay coalesced.
 //   gemm_tf32x3_kernel persistent (one CTA per SM, tiles of 128 x 128 taken
-//                      round robin), 192 threads: warp 0 issues TMA loads
+//                      round robin), 320 threads: warp 0 issues TMA loads
 //                      (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
 //                      of the four 128 x 32 slabs (A_hi, A_lo, B_hi, B_lo)
 //                      into a 3-stage ring with full / empty mbarriers; warp 1
 //                      allocates 2 x 128 TMEM columns and one thread issues 12
 //                      tcgen05.mma kind::tf32 (M = N = 128, K = 8) per slab,
-//                      committing each stage back to the producer; warps 2..5
-//                      move a finished accumulator out with tcgen05.ld.32x32b
-//                      (warp w reads TMEM lanes 32*(w%4)..) while the MMAs of
-//                      the next tile fill the other accumulator.
+//                      committing each stage back to the producer; the k range
+//                      of a tile is cut into chunks of CHUNK slabs, each
+//                      accumulated from zero in one of the two TMEM
+//                      accumulators (alternating), and warps 2..9 read every
+//                      finished chunk with tcgen05.ld.32x32b (warp w reads TMEM
+//                      lanes 32*(w%4).., columns 64*((w-2)/4)..) and add it
+//                      into f32 registers while the MMAs of the next chunk fill
+//                      the other accumulator; after the tile's last chunk they
+//                      store C.
 // Every mbarrier wait is bounded; on expiry the kernel records an error word
 // that om_b200_sync reports, and every warp leaves after its own bounded
 // waits so that TMEM is always freed.
@@ -40,10 +45,19 @@
 namespace om {
 namespace {
 
-constexpr int TM = 128, TN = 128, TK = 32, STAGES = 3, NTH = 192;
+constexpr int TM = 128, TN = 128, TK = 32, STAGES = 3, NTH = 320;
+constexpr int EPI_WARPS = 8;  // warps 2..9: lane quadrant (warp % 4), column half (warp - 2) / 4
 constexpr int SLAB_BYTES = TM * TK * 4;      // 16 KiB: 128 rows x 128 bytes
 constexpr int STAGE_BYTES = 4 * SLAB_BYTES;  // A_hi, A_lo, B_hi, B_lo
 constexpr uint32_t kWaitLimit = 1u << 24;    // polls of a try_wait before giving up
+// Slabs per accumulation chunk.  The tensor core adds the products of each
+// 8-deep MMA step into its f32 accumulator with its own (not round-to-nearest)
+// alignment and rounding, an error of the order of one ulp of the running
+// sum per step; over K = 1024 that bias reaches ~2^-16 of the partial sums.
+// Each chunk of CHUNK * 32 k is therefore accumulated in TMEM from zero and
+// added into f32 registers by the epilogue warps, which bounds the tensor
+// core's share of the error by CHUNK * 4 steps of a chunk-sized sum.
+constexpr int CHUNK = 4;
 
 // ---------------------------------------------------------------------------
 // split pre-pass
@@ -52,6 +66,8 @@ struct SplitArgs {
   const float* x;
   int64_t rows, K, Kp, batch;
   int64_t sr, sk, sb;  // element strides of (row, k, batch)
+  int64_t k1, sk2;     // k = k1-index + k1 * k2-index, read at k1i * sk + k2i * sk2
+  int64_t r1, sr2;     // rows likewise
   float* hi;
   float* lo;
 };
@@ -70,7 +86,9 @@ __global__ void split_tf32_kernel(SplitArgs a, int64_t tiles_k, int64_t tiles_r,
     const int64_t tk = t % tiles_k, rest = t / tiles_k;
     const int64_t tr = rest % tiles_r, b = rest / tiles_r;
     const int64_t r0 = tr * 32, k0 = tk * 32;
-    const float* xb = a.x + b * a.sb;
+    // a 32-wide tile never straddles an outer level (k1 % 32 == r1 % 32 == 0)
+    const int64_t ok_ = k0 / a.k1, or_ = r0 / a.r1;
+    const float* xb = a.x + (b * a.sb + ok_ * (a.sk2 - a.k1 * a.sk) + or_ * (a.sr2 - a.r1 * a.sr));
     __syncthreads();
     for (int i = ty; i < 32; i += 8) {
       const int64_t r = r0 + (k_fast ? i : tx), k = k0 + (k_fast ? tx : i);
@@ -174,6 +192,7 @@ __global__ void __launch_bounds__(NTH, 1)
   const int gx = (g.M + TM - 1) / TM, gy = (g.N + TN - 1) / TN;
   const int tiles = gx * gy * g.batch;
   const int G = gridDim.x;
+  const int nch = (g.T + CHUNK - 1) / CHUNK;
 
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -188,7 +207,8 @@ __global__ void __launch_bounds__(NTH, 1)
     }
     for (int b = 0; b < 2; ++b) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&tfull[b])));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(smem_u32(&tempty[b])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&tempty[b])),
+                   "r"(EPI_WARPS));
     }
     asm volatile("fence.mbarrier_init.release.cluster;");
   }
@@ -221,74 +241,91 @@ __global__ void __launch_bounds__(NTH, 1)
       if (!ok) atomicOr(g.err, 1u);
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // MMA issuer
+    if (lane == 0) {  // MMA issuer: one TMEM accumulator per k-chunk, alternating
       int q = 0, i = 0;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += G, ++i) {
-        const int ab = i & 1;
-        if (i >= 2) ok = mbar_wait(smem_u32(&tempty[ab]), ((i >> 1) - 1) & 1);
-        if (!ok) break;
-        asm volatile("tcgen05.fence::after_thread_sync;");
-        const uint32_t d = tmem + (uint32_t)(ab * TN);
-        for (int t = 0; t < g.T && ok; ++t, ++q) {
-          const int s = q % STAGES;
-          ok = mbar_wait(smem_u32(&full[s]), (q / STAGES) & 1);
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += G) {
+        for (int c = 0; c < nch && ok; ++c, ++i) {
+          const int ab = i & 1;
+          if (i >= 2) ok = mbar_wait(smem_u32(&tempty[ab]), ((i >> 1) - 1) & 1);
           if (!ok) break;
           asm volatile("tcgen05.fence::after_thread_sync;");
-          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t d = tmem + (uint32_t)(ab * TN);
+          const int t0 = c * CHUNK, t1 = min(g.T, t0 + CHUNK);
+          for (int t = t0; t < t1 && ok; ++t, ++q) {
+            const int s = q % STAGES;
+            ok = mbar_wait(smem_u32(&full[s]), (q / STAGES) & 1);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
-          for (int j = 0; j < TK / 8; ++j) {
-            const uint64_t a_h = sw128_desc(base + j * 32);
-            const uint64_t a_l = sw128_desc(base + SLAB_BYTES + j * 32);
-            const uint64_t b_h = sw128_desc(base + 2 * SLAB_BYTES + j * 32);
-            const uint64_t b_l = sw128_desc(base + 3 * SLAB_BYTES + j * 32);
-            mma_tf32(d, a_l, b_h, (t > 0 || j > 0) ? 1u : 0u);
-            mma_tf32(d, a_h, b_l, 1u);
-            mma_tf32(d, a_h, b_h, 1u);
+            for (int j = 0; j < TK / 8; ++j) {
+              const uint64_t a_h = sw128_desc(base + j * 32);
+              const uint64_t a_l = sw128_desc(base + SLAB_BYTES + j * 32);
+              const uint64_t b_h = sw128_desc(base + 2 * SLAB_BYTES + j * 32);
+              const uint64_t b_l = sw128_desc(base + 3 * SLAB_BYTES + j * 32);
+              mma_tf32(d, a_l, b_h, (t > t0 || j > 0) ? 1u : 0u);
+              mma_tf32(d, a_h, b_l, 1u);
+              mma_tf32(d, a_h, b_h, 1u);
+            }
+            mma_commit(smem_u32(&empty[s]));
           }
-          mma_commit(smem_u32(&empty[s]));
+          mma_commit(smem_u32(&tfull[ab]));  // fires when this chunk's MMAs are done
         }
-        mma_commit(smem_u32(&tfull[ab]));  // fires when this tile's MMAs are done
       }
       if (!ok) atomicOr(g.err, 1u);
     }
-  } else {  // epilogue warps 2..5: TMEM lanes 32*(warp % 4)
-    const int quad = warp & 3;
+  } else {  // epilogue warps 2..9: TMEM lanes 32*(warp % 4), columns 64*half..
+    const int quad = warp & 3, half = (warp - 2) >> 2;
+    constexpr int HN = TN / 2;
     int i = 0;
-    for (int tile = blockIdx.x; tile < tiles && ok; tile += G, ++i) {
-      const int ab = i & 1;
-      ok = mbar_wait(smem_u32(&tfull[ab]), (i >> 1) & 1);
-      if (!ok) break;
-      asm volatile("tcgen05.fence::after_thread_sync;");
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += G) {
       const int bx = tile % gx, by = (tile / gx) % gy, bt = tile / (gx * gy);
       const int m = bx * TM + 32 * quad + lane;
-      float* Cb = g.C + (int64_t)bt * g.scb;
-#pragma unroll 1
-      for (int c0 = 0; c0 < TN; c0 += 32) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(ab * TN + c0);
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
-            "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-              "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
-              "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
-              "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-              "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-              "=r"(r[30]), "=r"(r[31])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (m < g.M) {
+      // the tile's row m (this warp's half of it), summed chunk by chunk in
+      // f32 registers (round to nearest): the tensor core's own accumulation
+      // is only trusted over CHUNK slabs
+      float acc[HN];
 #pragma unroll
-          for (int qq = 0; qq < 32; ++qq) {
-            const int n = by * TN + c0 + qq;
-            if (n < g.N) Cb[(int64_t)m * g.scm + (int64_t)n * g.scn] = __uint_as_float(r[qq]);
-          }
+      for (int n = 0; n < HN; ++n) acc[n] = 0.f;
+      for (int c = 0; c < nch && ok; ++c, ++i) {
+        const int ab = i & 1;
+        ok = mbar_wait(smem_u32(&tfull[ab]), (i >> 1) & 1);
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        uint32_t r[HN];
+#pragma unroll
+        for (int c0 = 0; c0 < HN; c0 += 32) {
+          const uint32_t taddr =
+              tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(ab * TN + half * HN + c0);
+          uint32_t* x = r + c0;
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+              "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+              : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]),
+                "=r"(x[6]), "=r"(x[7]), "=r"(x[8]), "=r"(x[9]), "=r"(x[10]), "=r"(x[11]),
+                "=r"(x[12]), "=r"(x[13]), "=r"(x[14]), "=r"(x[15]), "=r"(x[16]), "=r"(x[17]),
+                "=r"(x[18]), "=r"(x[19]), "=r"(x[20]), "=r"(x[21]), "=r"(x[22]), "=r"(x[23]),
+                "=r"(x[24]), "=r"(x[25]), "=r"(x[26]), "=r"(x[27]), "=r"(x[28]), "=r"(x[29]),
+                "=r"(x[30]), "=r"(x[31])
+              : "r"(taddr));
+        }
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        // the accumulator is free as soon as it is in registers
+        asm volatile("tcgen05.fence::before_thread_sync;");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&tempty[ab]));
+#pragma unroll
+        for (int qq = 0; qq < HN; ++qq) acc[qq] += __uint_as_float(r[qq]);
+      }
+      if (!ok) break;
+      float* Cb = g.C + (int64_t)bt * g.scb;
+      if (m < g.M) {
+#pragma unroll
+        for (int n0 = 0; n0 < HN; ++n0) {
+          const int n = by * TN + half * HN + n0;
+          if (n < g.N) Cb[(int64_t)m * g.scm + (int64_t)n * g.scn] = acc[n0];
         }
       }
-      // hand the accumulator back to the MMA issuer
-      asm volatile("tcgen05.fence::before_thread_sync;");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&tempty[ab]));
     }
     if (!ok && lane == 0) atomicOr(g.err, 1u);
   }
@@ -330,8 +367,17 @@ int make_map(CUtensorMap* map, float* base, int64_t rows, int64_t Kp, int64_t ba
 }
 
 int launch_split(om_backend* be, const float* x, int64_t rows, int64_t K, int64_t Kp,
-                 int64_t batch, int64_t sr, int64_t sk, int64_t sb, float* hi, float* lo) {
-  SplitArgs a{x, rows, K, Kp, batch, sr, sk, sb, hi, lo};
+                 int64_t batch, int64_t sr, int64_t sk, int64_t sb, int64_t k1, int64_t sk2,
+                 int64_t r1, int64_t sr2, float* hi, float* lo) {
+  if (k1 <= 0) {  // flat: one level covering every k (and the padding)
+    k1 = Kp;
+    sk2 = 0;
+  }
+  if (r1 <= 0) {
+    r1 = (rows + 31) / 32 * 32;
+    sr2 = 0;
+  }
+  SplitArgs a{x, rows, K, Kp, batch, sr, sk, sb, k1, sk2, r1, sr2, hi, lo};
   const int64_t tk = Kp / 32, tr = (rows + 31) / 32, total = tk * tr * batch;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(total, (int64_t)be->num_sms * 16));
   ProfScope prof(be, "split_tf32");
@@ -342,13 +388,23 @@ int launch_split(om_backend* be, const float* x, int64_t rows, int64_t K, int64_
 
 }  // namespace
 
+bool tf32_takes(const om_backend* be, om_algebra alg, om_dtype dt, bool argmax, int64_t M,
+                int64_t N, int64_t K, int64_t batch) {
+  if (dt != OM_F32 || alg != OM_STANDARD || argmax || be->f32_exact) return false;
+  if (M < 64 || N < 64 || K < 16 || batch > 65535) return false;
+  if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return false;
+  const int64_t tiles = ((M + TM - 1) / TM) * ((N + TN - 1) / TN) * batch;
+  return tiles <= (1ll << 31) - 1;
+}
+
 // Takes a Standard f32 GEMM when the tensor-core path applies.
 int launch_gemm_tf32(om_backend* be, const GemmArgs& g, bool* handled) {
   *handled = false;
-  if (g.dtype != OM_F32 || g.alg != OM_STANDARD || g.argmax) return OM_OK;
-  if (g.M < 64 || g.N < 64 || g.K < 16 || g.batch > 65535) return OM_OK;
-  if (g.M > (1 << 30) || g.N > (1 << 30) || g.K > (1 << 30)) return OM_OK;
-  if (be->f32_exact) return OM_OK;
+  if (!tf32_takes(be, g.alg, g.dtype, g.argmax != nullptr, g.M, g.N, g.K, g.batch)) {
+    if (g.ka1 > 0 || g.kb1 > 0 || g.ma1 > 0 || g.nb1 > 0)
+      return set_error(OM_ERR_INVALID, "gemm: two-level index off the tensor-core path");
+    return OM_OK;
+  }
   const int64_t Kp = (g.K + TK - 1) / TK * TK;
   const size_t na = (size_t)(g.batch * g.M * Kp), nb = (size_t)(g.batch * g.N * Kp);
   Scratch ws;
@@ -357,8 +413,10 @@ int launch_gemm_tf32(om_backend* be, const GemmArgs& g, bool* handled) {
   float* a_lo = a_hi + na;
   float* b_hi = a_lo + na;
   float* b_lo = b_hi + nb;
-  OM_TRY(launch_split(be, (const float*)g.A, g.M, g.K, Kp, g.batch, g.sam, g.sak, g.sab, a_hi, a_lo));
-  OM_TRY(launch_split(be, (const float*)g.B, g.N, g.K, Kp, g.batch, g.sbn, g.sbk, g.sbb, b_hi, b_lo));
+  OM_TRY(launch_split(be, (const float*)g.A, g.M, g.K, Kp, g.batch, g.sam, g.sak, g.sab, g.ka1,
+                      g.sak2, g.ma1, g.sam2, a_hi, a_lo));
+  OM_TRY(launch_split(be, (const float*)g.B, g.N, g.K, Kp, g.batch, g.sbn, g.sbk, g.sbb, g.kb1,
+                      g.sbk2, g.nb1, g.sbn2, b_hi, b_lo));
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   OM_TRY(make_map(&m_ahi, a_hi, g.M, Kp, g.batch));
   OM_TRY(make_map(&m_alo, a_lo, g.M, Kp, g.batch));
@@ -379,7 +437,6 @@ int launch_gemm_tf32(om_backend* be, const GemmArgs& g, bool* handled) {
           "cudaFuncSetAttribute(tf32)");
   a.batch = (int)g.batch;
   const int64_t tiles = (int64_t)((a.M + TM - 1) / TM) * ((a.N + TN - 1) / TN) * g.batch;
-  if (tiles > (1ll << 31) - 1) return OM_OK;
   const unsigned grid = (unsigned)std::min<int64_t>(tiles, be->num_sms);
   {
     ProfScope prof(be, "gemm_tf32x3_tcgen05");

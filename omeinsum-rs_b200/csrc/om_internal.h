@@ -124,8 +124,18 @@ struct GemmArgs {
   // When set, the exact kernel runs only if the special-value scan of the
   // fast tropical path (bits in *fast_gate) rules the fast path out.
   const uint32_t* fast_gate = nullptr;
+  // Two-level indices, only for the tensor-core Standard f32 path
+  // (tf32_takes): k = k1 + ka1 * k2 reads A at k1 * sak + k2 * sak2 (ka1 a
+  // multiple of 32; ka1 == 0 means the flat stride sak), and likewise for
+  // B's k (kb1, sbk2), A's rows (ma1, sam2) and B's columns (nb1, sbn2).
+  int64_t ka1 = 0, sak2 = 0, kb1 = 0, sbk2 = 0;
+  int64_t ma1 = 0, sam2 = 0, nb1 = 0, sbn2 = 0;
 };
 int launch_gemm(om_backend* be, const GemmArgs& g);
+// Whether launch_gemm gives this Standard f32 problem to the tensor-core
+// kernel (the only kernel that reads a two-level contracted index).
+bool tf32_takes(const om_backend* be, om_algebra alg, om_dtype dt, bool argmax, int64_t M,
+                int64_t N, int64_t K, int64_t batch);
 
 // Unsigned 32-bit division by an invariant divisor d >= 1 with one
 // multiply-high, exact for every dividend below 2^32 (Granlund & Montgomery,
