@@ -166,27 +166,51 @@ def run_reference(args, rank, world):
 
 
 def run_permuted(be, om, local_rank):
-    """'abcd,dcef->abfe', a=b=e=f=64, c=d=32, f32 N(0,1),
-    as Standard (tensor cores, 3xTF32) and as MinPlus; device-timed per
-    om_b200_contract call (kernels per class from the profiler)."""
+    """'abcd,dcef->abfe', a=b=e=f=64, c=d=32, f32 N(0,1):
+    Standard on the tensor cores (3xTF32) and on the CUDA cores (exact f32
+    FMA), and MinPlus; device-timed per om_b200_contract call (kernels per
+    class from the profiler), each output checked on sampled rows against
+    the oracle first (Standard under the f32 rule, MinPlus bit-exact)."""
     import oracle as orc
     import torch
     a_, c_ = 64, 32
     sa, sb = [a_, a_, c_, c_], [c_, c_, a_, a_]
-    A = be.from_slice(orc.normal(SEED + 2, a_ * a_ * c_ * c_))
-    B = be.from_slice(orc.normal(SEED + 3, c_ * c_ * a_ * a_))
+    ha, hb = orc.normal(SEED + 2, a_ * a_ * c_ * c_), orc.normal(SEED + 3, c_ * c_ * a_ * a_)
+    A, B = be.from_slice(ha), be.from_slice(hb)
     C = be.alloc(a_ ** 4, np.float32)
     col = om.col_strides
     flops = 2.0 * 4096 * 4096 * 1024
     out = {"workload": "abcd,dcef->abfe a=b=e=f=64 c=d=32 f32", "unit": "TFLOP/s (TOP/s)"}
     stream = torch.cuda.ExternalStream(be.stream(), device=local_rank)
-    for alg in ("standard", "minplus"):
+    rows = np.array([0, 1, 777, 2048, 4095])
+    sub = np.ascontiguousarray(ha.reshape(c_ * c_, a_ * a_)[:, rows].T).reshape(-1, order="F")
+    ssub = [len(rows), c_, c_]
+    for alg, mode in (("standard", "3xtf32"), ("standard", "exact"), ("minplus", None)):
+        if mode:
+            be.set_f32_mode(mode)
+
         def call():
             be.contract_into(alg, A, sa, col(sa), [0, 1, 2, 3], B, sb, col(sb), [3, 2, 4, 5],
                              [a_] * 4, [0, 1, 5, 4], C, None)
         for _ in range(3):
             call()
         be.synchronize()
+        # sampled-row check of this mode's output
+        got = C.to_vec().reshape(a_ * a_, a_ * a_, order="F")[rows, :]
+        if alg == "standard":
+            r = orc.contract("standard", sub.astype(np.float64), ssub, col(ssub), [100, 2, 3],
+                             hb.astype(np.float64), sb, col(sb), [3, 2, 4, 5],
+                             [len(rows), a_, a_], [100, 5, 4]).reshape(len(rows), -1, order="F")
+            bound = np.maximum(1e-5 * np.abs(r), np.max(np.abs(r)) * 32 * 2.0 ** -23)
+            err = float(np.max(np.abs(got - r) / bound))
+            check = {"rule": "|x-r| <= max(1e-5|r|, ||r||_inf sqrt(K) 2^-23)",
+                     "max_err_over_bound": round(err, 4), "ok": err <= 1.0}
+        else:
+            r = orc.contract("minplus", sub, ssub, col(ssub), [100, 2, 3], hb, sb, col(sb),
+                             [3, 2, 4, 5], [len(rows), a_, a_], [100, 5, 4])
+            ok = np.array_equal(got.view(np.uint32),
+                                r.reshape(len(rows), -1, order="F").view(np.uint32))
+            check = {"rule": "bit-exact", "ok": bool(ok)}
         be.profile(True)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 10
@@ -198,16 +222,24 @@ def run_permuted(be, om, local_rank):
         ms = e0.elapsed_time(e1) / reps
         prof = be.profile_report()
         be.profile(False)
-        out[alg] = {"ms_per_call": round(ms, 4), "value": round(flops / (ms / 1e3) / 1e12, 2),
-                    "kernels_ms": {k: round(v[0] / v[1], 4) for k, v in prof.items()}}
+        key = alg if mode is None else f"{alg}_{mode}"
+        out[key] = {"ms_per_call": round(ms, 4), "value": round(flops / (ms / 1e3) / 1e12, 2),
+                    "kernels_ms": {k: round(v[0] / v[1], 4) for k, v in prof.items()},
+                    "check_sampled_rows": check}
+    be.set_f32_mode("3xtf32")
     return out
 
 
 NET_N = 190
 NET_SLICED = int(os.environ.get("OM_BENCH_NET_SLICED", "6"))
+HBM_GBS = 6534.5  # MEASURED_PEAKS.json hbm_gbs (copy kernel, this pool's B200s)
 
 
-def run_network(be, om, world, rank, local_rank, args, nsliced=None):
+def _events(torch, n):
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def run_network(be, om, world, rank, local_rank, args, nsliced=None, cpu=False):
     """BASELINE config 4's method: MIS on a seeded 3-regular graph, MaxPlus
     f32, NET_SLICED sliced labels (2^NET_SLICED slices, 64 by default, so
     every rank has 8 at N = 8) spread over the ranks, combined by an NCCL
@@ -235,7 +267,7 @@ def run_network(be, om, world, rank, local_rank, args, nsliced=None):
     ex.value_and_grad(assigns[0])  # every rank records its gradient graph before timing
     reps = 3
     stream = torch.cuda.ExternalStream(be.stream(), device=local_rank)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0, t1 = _events(torch, 2)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -249,7 +281,7 @@ def run_network(be, om, world, rank, local_rank, args, nsliced=None):
     torch.cuda.synchronize()
     ms = torch.tensor([t0.elapsed_time(t1) / reps], dtype=torch.float64, device=dev)
     # the two kinds of slice work, timed apart on this rank (diagnostic)
-    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0, e1, e2 = _events(torch, 3)
     e0.record(stream)
     ex.value(assigns[0])
     e1.record(stream)
@@ -261,17 +293,134 @@ def run_network(be, om, world, rank, local_rank, args, nsliced=None):
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     sel = [int(x[1] > x[0]) for x in g[:NET_N]]
     valid = sum(sel) == int(v) and all(not (sel[a] and sel[b]) for a, b in edges)
-    return {"workload": f"mis_3regular_n{NET_N}_maxplus_f32_{2 ** nsliced}_slices_argmax_backward",
-            "metric": "network contract wall-time", "unit": "ms", "higher_is_better": False,
-            "value": round(float(ms.item()), 3), "n_gpus": world, "scaling": "strong",
-            "mis_size": v, "configuration_valid": bool(valid), "winning_slice": int(win),
-            "log2_tc": round(float(np.log2(tc)), 2), "log2_sc": round(float(np.log2(sc)), 2),
-            "per_slice_log2_tc": round(float(np.log2(tcs)), 2),
-            "per_slice_log2_sc": round(float(np.log2(scs)), 2),
-            "slices": 2 ** nsliced, "slice_value_ms": round(value_ms, 3),
-            "slice_value_and_grad_ms": round(grad_ms, 3),
-            "order": "min-fill elimination, best of 8 seeded restarts (omeco TreeSA unavailable)",
-            "timing": "CUDA events on the backend stream around 3 full runs, max over ranks"}
+    nbytes = N.slice_node_bytes(tree, ixs, iy, sizes, sliced, 4, E.tree_output_labels)
+    achieved = nbytes / (value_ms / 1e3) / 1e9
+    out = {"workload": f"mis_3regular_n{NET_N}_maxplus_f32_{2 ** nsliced}_slices_argmax_backward",
+           "metric": "network contract wall-time", "unit": "ms", "higher_is_better": False,
+           "value": round(float(ms.item()), 3), "n_gpus": world, "scaling": "strong",
+           "mis_size": v, "configuration_valid": bool(valid), "winning_slice": int(win),
+           "log2_tc": round(float(np.log2(tc)), 2), "log2_sc": round(float(np.log2(sc)), 2),
+           "per_slice_log2_tc": round(float(np.log2(tcs)), 2),
+           "per_slice_log2_sc": round(float(np.log2(scs)), 2),
+           "slices": 2 ** nsliced, "slice_value_ms": round(value_ms, 3),
+           "slice_value_and_grad_ms": round(grad_ms, 3),
+           "roofline": {"bound": "hbm", "bytes_per_slice": int(nbytes),
+                        "achieved_gbs": round(achieved, 1), "peak_gbs": HBM_GBS,
+                        "frac": round(achieved / HBM_GBS, 4),
+                        "note": "operands read once + outputs written once over the nodes a "
+                                "slice runs, / slice_value_ms; peak of measured (copy)"},
+           "order": "min-fill elimination, best of 8 seeded restarts (omeco TreeSA unavailable)",
+           "timing": "CUDA events on the backend stream around 3 full runs, max over ranks"}
+    if cpu and rank == 0 and world == 1:
+        import engine as oe
+        ox = N.OracleExecutor(oe, E, "maxplus", ixs, iy, sizes, ts, tree)
+        t = time.perf_counter()
+        ov = ox.value(assigns[win])
+        dt = time.perf_counter() - t
+        assert ov == ex.value(assigns[win]), "network check"
+        out["cpu_baseline"] = {"value": round(dt * 1e3 * len(assigns), 1), "unit": "ms",
+                               "cores": 1, "kind": "port",
+                               "sample": f"oracle engine, value of slice {win} ({dt:.1f} s) x "
+                                         f"{len(assigns)} slices; the gradient is left out"}
+    return out
+
+
+def run_config3(be, om, local_rank, cpu=False):
+    """MIS on a seeded 3-regular graph with 150 vertices,
+    MaxPlus f32, greedy order, value and argmax backward (the configuration)
+    on one GPU through the engine (om_b200_einsum + backward)."""
+    import importlib
+    import torch
+    E = importlib.import_module("omeinsum_b200.einsum")
+    ixs, iy, sizes, ts, edges = E.mis_network(150, SEED)
+    ein = E.Einsum(ixs, iy, sizes).optimize_greedy()
+    tc, sc = E.tree_cost(ein.tree, ixs, iy, sizes)
+    dev = [be.from_slice(t) for t in ts]
+    stream = torch.cuda.ExternalStream(be.stream(), device=local_rank)
+    for _ in range(2):
+        c, g = ein.cost_and_gradient(be, "maxplus", dev, dy=[1.0])
+    be.synchronize()
+    reps = 5
+    e0, e1 = _events(torch, 2)
+    e0.record(stream)
+    for _ in range(reps):
+        c, g = ein.cost_and_gradient(be, "maxplus", dev, dy=[1.0])
+    e1.record(stream)
+    be.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    val = float(c.to_vec()[0])
+    sel = [int(x.to_vec()[1] > 0) for x in g[:150]]
+    valid = sum(sel) == int(val) and all(not (sel[u] and sel[v]) for u, v in edges)
+    out = {"workload": "mis_3regular_n150_maxplus_f32_greedy_value_and_argmax_backward",
+           "metric": "network contract wall-time", "unit": "ms", "higher_is_better": False,
+           "value": round(ms, 3), "mis_size": val, "configuration_valid": bool(valid),
+           "log2_tc": round(float(np.log2(tc)), 2), "log2_sc": round(float(np.log2(sc)), 2),
+           "timing": "CUDA events on the backend stream around 5 value+gradient calls"}
+    if cpu:
+        import engine as oe
+        ch, niy = ein.encoded()
+        t = time.perf_counter()
+        rc, _ = oe.cost_and_gradient("maxplus", ts, ixs, iy, sizes, ch, niy,
+                                     np.ones(1, np.float32))
+        dt = time.perf_counter() - t
+        assert float(rc[0]) == val, "config 3 check"
+        out["cpu_baseline"] = {"value": round(dt * 1e3, 1), "unit": "ms", "cores": 1,
+                               "kind": "port",
+                               "sample": "oracle engine, whole value + argmax backward, same tree"}
+    return out
+
+
+def run_config5(be, om, world, rank, local_rank, cpu=False):
+    """Ising spin glass on a seeded 3-regular graph with
+    120 vertices, Standard f64, beta = 1, J ~ N(0, 1), 3 sliced labels (8
+    slices) over the ranks, Z and dZ/dT for every edge tensor, combined by an
+    NCCL sum all-reduce on the device."""
+    import importlib
+    import torch
+    E = importlib.import_module("omeinsum_b200.einsum")
+    N = importlib.import_module("omeinsum_b200.network")
+    ixs, iy, sizes, ts, edges = E.ising_network(120, SEED)
+    tree = E.best_tree(ixs, iy, sizes, restarts=8)
+    sliced = N.choose_slices(ixs, iy, sizes, tree, 3, E.tree_cost)
+    tc, sc = E.tree_cost(tree, ixs, iy, sizes)
+    ex = N.DeviceExecutor(be, E, "standard", ixs, iy, sizes, ts, tree)
+    dist = torch.distributed if world > 1 else None
+    dev = torch.device(f"cuda:{local_rank}")
+    for _ in range(2):
+        N.run_sliced(ex, "standard", ixs, sizes, sliced, rank, world, dist=dist, device=dev)
+    stream = torch.cuda.ExternalStream(be.stream(), device=local_rank)
+    reps = 5
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    be.synchronize()
+    e0, e1 = _events(torch, 2)
+    e0.record(stream)
+    for _ in range(reps):
+        z, g, _ = N.run_sliced(ex, "standard", ixs, sizes, sliced, rank, world, dist=dist,
+                               device=dev)
+    e1.record(stream)
+    be.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    out = {"workload": "ising_3regular_n120_standard_f64_8_slices_z_and_edge_gradients",
+           "metric": "network contract wall-time", "unit": "ms", "higher_is_better": False,
+           "value": round(float(ms.item()), 3), "n_gpus": world, "scaling": "strong",
+           "log_z": round(float(np.log(z)), 6), "edges_with_gradient": len(g),
+           "log2_tc": round(float(np.log2(tc)), 2), "log2_sc": round(float(np.log2(sc)), 2),
+           "timing": "CUDA events on the backend stream around 5 full runs, max over ranks"}
+    if cpu and rank == 0 and world == 1:
+        import engine as oe
+        ox = N.OracleExecutor(oe, E, "standard", ixs, iy, sizes, ts, tree)
+        t = time.perf_counter()
+        oz, og, _ = N.run_sliced(ox, "standard", ixs, sizes, sliced, 0, 1)
+        dt = time.perf_counter() - t
+        assert abs(oz - z) <= 1e-12 * abs(oz), "config 5 check"
+        out["cpu_baseline"] = {"value": round(dt * 1e3, 1), "unit": "ms", "cores": 1,
+                               "kind": "port",
+                               "sample": "oracle engine, all 8 slices with gradients, same tree"}
+    return out
 
 
 def run_b200(args, rank, world, local_rank):
@@ -366,9 +515,12 @@ def run_b200(args, rank, world, local_rank):
     e2e_value = world * args.steps * OPS / float(t_e2e.item()) / 1e9
 
     permuted = run_permuted(be, om, local_rank) if rank == 0 else None
-    network = run_network(be, om, world, rank, local_rank, args)
+    cpu_nets = world == 1 and not args.no_cpu
+    network = run_network(be, om, world, rank, local_rank, args, cpu=cpu_nets)
     # config 4 as written: 3 sliced labels, 8 slices
     network8 = run_network(be, om, world, rank, local_rank, args, nsliced=3)
+    config5 = run_config5(be, om, world, rank, local_rank, cpu=cpu_nets)
+    config3 = run_config3(be, om, local_rank, cpu=cpu_nets) if rank == 0 else None
     if rank != 0:
         return
     # roofline of the dominant kernel (device time per launch from the events)
@@ -411,6 +563,8 @@ def run_b200(args, rank, world, local_rank):
         "clocks": clk.summary(),
         "network": network,
         "network_8_slices": network8,
+        "ising_n120_f64_sliced_grad": config5,
+        "config3_mis_n150": config3,
         "permuted": permuted,
     }
     print(json.dumps(line), flush=True)
@@ -424,7 +578,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-check", action="store_true")
-    ap.add_argument("--case", default="headline", choices=["headline", "config2", "contract", "network", "slices"],
+    ap.add_argument("--no-cpu", action="store_true", help="leave out the network CPU baselines")
+    ap.add_argument("--case", default="headline", choices=["headline", "config2", "contract", "network", "slices",
+                             "networks"],
                     help="profiling cases: config2 = only the config-2 permuted "
                          "contraction; contract = only warmup + steps headline calls; "
                          "network = only the sliced MIS network, with its kernel breakdown; "
@@ -442,6 +598,21 @@ def main():
         torch.cuda.set_device(local_rank)
         be = om.B200(local_rank)
         print(json.dumps(run_permuted(be, om, local_rank)), flush=True)
+        be.close()
+        return
+    if args.case == "networks" and world == 1:
+        import torch
+        om = load_pkg()
+        torch.cuda.set_device(local_rank)
+        be = om.B200(local_rank)
+        be.profile(True)
+        out = {"config5": run_config5(be, om, 1, 0, local_rank),
+               "config3": run_config3(be, om, local_rank)}
+        prof = be.profile_report()
+        be.profile(False)
+        out["kernels_ms_total"] = {k: [round(v[0], 3), v[1]] for k, v in
+                                   sorted(prof.items(), key=lambda kv: -kv[1][0])}
+        print(json.dumps(out), flush=True)
         be.close()
         return
     if args.case == "network" and world == 1:

@@ -433,10 +433,111 @@ int launch_gemm_exact(om_backend* be, const GemmArgs& g) {
   return set_error(OM_ERR_UNSUPPORTED, "gemm: dtype must be f32 or f64");
 }
 
+// A node with few outputs and a long contracted range (the root of a network
+// is often a dot product of two large intermediates): one CTA per output,
+// each thread reduces a contiguous run of k, and thread 0 combines the runs
+// in k order.  The tropical combine reproduces the sequential rule of
+// generic_gemm_with_argmax exactly: a run is summarised by its first best
+// element taken from an empty start (what the sequential rule holds after the
+// run from any incoming value it replaces), or, when the run holds a NaN
+// product, by the state after its last NaN (which no earlier value survives).
+constexpr int kSplitThreads = 256;
+
+template <typename T, int ALG, bool ARGMAX>
+__global__ void __launch_bounds__(kSplitThreads) gemm_node_splitk(NodeArgs g) {
+  using S = Semi<ALG, T>;
+  __shared__ T sv[kSplitThreads];
+  __shared__ uint32_t si[kSplitThreads];
+  __shared__ uint8_t sf[kSplitThreads];  // bit 0: run not empty, bit 1: run reset by a NaN
+  const int tid = threadIdx.x;
+  const T* __restrict__ A = (const T*)g.A;
+  const T* __restrict__ B = (const T*)g.B;
+  for (int64_t o = blockIdx.x; o < g.total; o += gridDim.x) {
+    int64_t oa = 0, ob = 0;
+    {
+      uint32_t r = (uint32_t)o;
+      for (int j = 0; j < g.nout; ++j) {
+        const uint32_t q = fast_div(r, g.out[j].div);
+        const uint32_t d = r - q * g.out[j].div.d;
+        oa += (int64_t)d * g.out[j].sa;
+        ob += (int64_t)d * g.out[j].sb;
+        r = q;
+      }
+    }
+    const int64_t per = (g.K + kSplitThreads - 1) / kSplitThreads;
+    const int64_t k0 = tid * per, k1 = k0 + per < g.K ? k0 + per : g.K;
+    T acc = ALG == OM_STANDARD ? T(0) : S::zero();
+    uint32_t idx = 0;
+    uint8_t flag = 0;
+    for (int64_t k = k0; k < k1; ++k) {
+      uint32_t r = (uint32_t)k;
+      int64_t xa = oa, xb = ob;
+      for (int j = 0; j < g.nk; ++j) {
+        const uint32_t q = fast_div(r, g.kmodes[j].div);
+        const uint32_t d = r - q * g.kmodes[j].div.d;
+        xa += (int64_t)d * g.kmodes[j].sa;
+        xb += (int64_t)d * g.kmodes[j].sb;
+        r = q;
+      }
+      if (ALG == OM_STANDARD) {
+        acc = fma(A[xa], B[xb], acc);
+      } else {
+        const T p = S::mul(A[xa], B[xb]);
+        if (!(flag & 1) || !S::keep(acc, p)) {
+          acc = p;
+          idx = (uint32_t)k;
+        }
+        flag |= 1;
+        if (p != p) flag |= 2;
+      }
+    }
+    sv[tid] = acc;
+    si[tid] = idx;
+    sf[tid] = flag;
+    __syncthreads();
+    if (tid == 0) {
+      T v = ALG == OM_STANDARD ? T(0) : S::zero();
+      uint32_t w = 0;
+      for (int t = 0; t < kSplitThreads; ++t) {
+        if (ALG == OM_STANDARD) {
+          v += sv[t];
+        } else if (sf[t] & 2) {
+          v = sv[t];
+          w = si[t];
+        } else if ((sf[t] & 1) && !S::keep(v, sv[t])) {
+          v = sv[t];
+          w = si[t];
+        }
+      }
+      ((T*)g.C)[o] = v;
+      if (ARGMAX) g.argmax[o] = w;
+    }
+    __syncthreads();
+  }
+}
+
 int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
   if (g0.total <= 0) return OM_OK;
   if (g0.K >= (int64_t(1) << 32) || g0.nout > kMaxNodeModes || g0.nk > kMaxNodeModes)
     return set_error(OM_ERR_INVALID, "gemm_node: plan out of range");
+  if (g0.K >= 2048 && g0.total <= 4 * (int64_t)be->num_sms) {
+    // few outputs, long k: split the k range of each output over a CTA
+    const int grid = (int)g0.total;
+    ProfScope prof(be, "gemm_node_splitk");
+    if (g0.dtype == OM_F32) {
+      OM_DISPATCH_ALG(g0.alg, ALG, {
+        if (g0.argmax) gemm_node_splitk<float, ALG, true><<<grid, kSplitThreads, 0, be->stream>>>(g0);
+        else gemm_node_splitk<float, ALG, false><<<grid, kSplitThreads, 0, be->stream>>>(g0);
+      });
+    } else {
+      OM_DISPATCH_ALG(g0.alg, ALG, {
+        if (g0.argmax) gemm_node_splitk<double, ALG, true><<<grid, kSplitThreads, 0, be->stream>>>(g0);
+        else gemm_node_splitk<double, ALG, false><<<grid, kSplitThreads, 0, be->stream>>>(g0);
+      });
+    }
+    note_launch();
+    return check_cuda(cudaGetLastError(), "gemm_node_splitk launch");
+  }
   // V = 4 outputs per thread when the first output mode splits into groups
   // of four and the outputs take 16-byte stores; the tile row then spans up
   // to 4 * kNodeQuads outputs

@@ -620,20 +620,37 @@ __device__ __forceinline__ uint32_t classify_bits(uint32_t u, uint32_t pinf_bit,
 
 // one CTA per group of runs, float4 loads along each run
 __global__ void special_scan_kernel(ScanArgs s0, ScanArgs s1, uint32_t* flags) {
+  // one flat index space of 16-byte vectors per operand (line-major), walked
+  // grid-stride with four independent loads in flight per thread, so short
+  // lines do not leave threads idle
   uint32_t f = 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
 #pragma unroll
   for (int w = 0; w < 2; ++w) {
     const ScanArgs& s = w ? s1 : s0;
-    const int vec = s.inner / 4;
-    for (int64_t l = blockIdx.x; l < s.lines; l += gridDim.x) {
-      const float4* run = (const float4*)(s.p + (l % s.outer) * s.ld + (l / s.outer) * s.bs);
-      for (int v = threadIdx.x; v < vec; v += blockDim.x) {
-        const float4 x = run[v];
-        f |= classify_bits(__float_as_uint(x.x), s.pinf_bit, s.ninf_bit) |
-             classify_bits(__float_as_uint(x.y), s.pinf_bit, s.ninf_bit) |
-             classify_bits(__float_as_uint(x.z), s.pinf_bit, s.ninf_bit) |
-             classify_bits(__float_as_uint(x.w), s.pinf_bit, s.ninf_bit);
-      }
+    const int64_t vec = s.inner / 4, total = vec * s.lines;
+    auto at = [&](int64_t i) {
+      const int64_t l = i / vec, v = i - l * vec;
+      return ((const float4*)(s.p + (l % s.outer) * s.ld + (l / s.outer) * s.bs))[v];
+    };
+    int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < total; i += 4 * stride) {
+      float4 x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = at(i + u * stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        f |= classify_bits(__float_as_uint(x[u].x), s.pinf_bit, s.ninf_bit) |
+             classify_bits(__float_as_uint(x[u].y), s.pinf_bit, s.ninf_bit) |
+             classify_bits(__float_as_uint(x[u].z), s.pinf_bit, s.ninf_bit) |
+             classify_bits(__float_as_uint(x[u].w), s.pinf_bit, s.ninf_bit);
+    }
+    for (; i < total; i += stride) {
+      const float4 x = at(i);
+      f |= classify_bits(__float_as_uint(x.x), s.pinf_bit, s.ninf_bit) |
+           classify_bits(__float_as_uint(x.y), s.pinf_bit, s.ninf_bit) |
+           classify_bits(__float_as_uint(x.z), s.pinf_bit, s.ninf_bit) |
+           classify_bits(__float_as_uint(x.w), s.pinf_bit, s.ninf_bit);
     }
   }
   f = __reduce_or_sync(0xffffffffu, f);
@@ -731,10 +748,11 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
   sb.lines = (int64_t)sb.outer * g.batch;
   sb.pinf_bit = SV_B_PINF;
   sb.ninf_bit = SV_B_NINF;
-  const int blocks = (int)std::min<int64_t>(std::max(sa.lines, sb.lines), (int64_t)be->num_sms * 8);
+  const int64_t vecs = std::max(sa.lines * (sa.inner / 4), sb.lines * (sb.inner / 4));
+  const int blocks = (int)std::min<int64_t>((vecs + 255) / 256, (int64_t)be->num_sms * 8);
   {
     ProfScope prof(be, "special_scan");
-    special_scan_kernel<<<std::max(blocks, 1), 128, 0, be->stream>>>(sa, sb, be->d_flags);
+    special_scan_kernel<<<std::max(blocks, 1), 256, 0, be->stream>>>(sa, sb, be->d_flags);
     note_launch();
     OM_CUDA(cudaGetLastError(), "special_scan launch");
   }

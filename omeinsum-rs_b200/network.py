@@ -49,6 +49,37 @@ def choose_slices(ixs, iy, sizes, tree, k, tree_cost):
     return chosen
 
 
+def slice_node_bytes(tree, ixs, iy, sizes, sliced, itemsize, tree_output_labels):
+    """Algorithmic bytes of one slice: for every node whose subtree holds a
+    sliced label (the nodes a slice runs; the others are contracted once for
+    all slices), both operands read once and the output written once, at the
+    slice's extents (sliced labels have extent 1)."""
+    sl = set(sliced)
+    labels = tree_output_labels(tree, ixs, iy)
+    s1 = {l: (1 if l in sl else v) for l, v in sizes.items()}
+
+    def size(ls):
+        n = 1
+        for l in ls:
+            n *= s1[l]
+        return n
+
+    total = 0
+
+    def rec(t):
+        nonlocal total
+        if isinstance(t, int):
+            return list(dict.fromkeys(ixs[t])), bool(set(ixs[t]) & sl)
+        (a, da), (b, db) = rec(t[0]), rec(t[1])
+        out = labels[id(t)]
+        if da or db:
+            total += (size(a) + size(b) + size(out)) * itemsize
+        return out, da or db
+
+    rec(tree)
+    return total
+
+
 def slice_assignments(sliced, sizes):
     """All assignments of the sliced labels, slice id = column-major index."""
     ranges = [range(sizes[l]) for l in sliced]
@@ -266,21 +297,12 @@ class DeviceExecutor:
         self._run(plan, assign)
         return float(plan["out"].to_vec()[0])
 
-    def _grad_plan(self, assign):
-        """The reduced tree of the value plan (same fixed buffers), its
-        forward with tape recorded once as a graph; the tape stays valid
-        across replays.  Gradients reaching a hoisted leaf continue through
-        the tape its subtree was contracted with."""
-        key = frozenset(assign.keys())
-        gp = self._grad_plans.get(key)
-        if gp is not None:
-            return gp
-        plan = self._ensure_plan(assign)
-        ein = plan["ein"]
-        out = self.be.alloc(ein.out_size(), self.dtype)
-        # every gradient lives in one buffer: first the input tensors' (the
-        # reduced tree's plain leaves, then each hoisted subtree's leaves --
-        # the order of _gbuf_order), then the hoisted intermediates' own
+    def _grad_buffers(self, plan, key):
+        """One device buffer for every gradient of a slice: first the input
+        tensors' (the reduced tree's plain leaves, then each hoisted
+        subtree's leaves -- the order of _gbuf_order), then the hoisted
+        intermediates' own.  Returns (grads per reduced leaf, grads per
+        hoisted subtree leaf, the buffer, end of the input part)."""
         leaves = self._reduce(key)[0]
         om = sys.modules[type(self.be).__module__]
         sizes_red = [max(1, int(np.prod(v[1]))) for v in plan["views"]]
@@ -304,6 +326,81 @@ class DeviceExecutor:
             if lf[0] == "hoisted":
                 grads[j] = om.View(gbuf, at, n)
                 at += n
+        return grads, sub_grads, gbuf, inputs_end
+
+    def _std_plan(self, assign, layout):
+        """Standard algebra: one recorded graph per set of sliced labels that
+        runs a slice's forward with tape, the backward through it and the
+        hoisted subtrees' tapes, and adds value and gradients into a fixed
+        accumulator ([value, full gradients], placed through a fixed index
+        buffer that each slice refills).  A slice then costs its staging
+        copies, one index copy and one graph launch."""
+        key = frozenset(assign.keys())
+        sp = self.__dict__.setdefault("_std_plans", {}).get(key)
+        if sp is not None:
+            return sp
+        om = sys.modules[type(self.be).__module__]
+        L = om.lib()
+        dt = om.DTYPES[np.dtype(self.dtype)]
+        plan = self._ensure_plan(assign)
+        ein = plan["ein"]
+        grads, sub_grads, gbuf, inputs_end = self._grad_buffers(plan, key)
+        leaves = self._reduce(key)[0]
+        links = [(j, lf[3], sg) for j, (lf, sg) in enumerate(zip(leaves, sub_grads))
+                 if lf[0] == "hoisted"]
+        sp = {"out": self.be.alloc(ein.out_size(), self.dtype),
+              "dy": self.be.from_slice(np.ones(1, self.dtype)),
+              "idx": self.be.alloc(inputs_end, np.int64),
+              "zero_idx": self.be.from_slice(np.zeros(1, np.int64)),
+              "acc": self.be.alloc(1 + layout.total, self.dtype),
+              "grads": grads, "sub_grads": sub_grads, "gbuf": gbuf, "n": inputs_end,
+              "layout": layout, "tape": None}
+        self.be.graph_begin()
+        try:
+            sp["tape"] = ein.forward_tape_views(self.be, self.alg, plan["tensors"], plan["views"],
+                                                sp["out"])
+            ein.backward_tape(sp["tape"], sp["dy"], grads)
+            for j, sub_tape, sg in links:
+                self.E.Einsum.backward_tape(sub_tape, grads[j], sg)
+            om._check(L.om_b200_scatter_index(self.be.h, dt, gbuf.ptr, inputs_end,
+                                              sp["idx"].ptr, sp["acc"].ptr, 1))
+            om._check(L.om_b200_scatter_index(self.be.h, dt, sp["out"].ptr, 1,
+                                              sp["zero_idx"].ptr, sp["acc"].ptr, 1))
+        finally:
+            sp["graph"] = self.be.graph_end()
+        self._std_plans[key] = sp
+        return sp
+
+    def std_sum(self, assigns, layout):
+        """Standard algebra: the sum over `assigns` of [value, full gradients]
+        on the device (the plan's accumulator, zeroed first)."""
+        if not assigns:
+            return None
+        sp = self._std_plan(assigns[0], layout)
+        if sp["layout"] is not layout:
+            raise ValueError("std_sum: one layout per executor and set of sliced labels")
+        plan = self._ensure_plan(assigns[0])
+        self.be.upload_into(sp["acc"], np.zeros(1 + layout.total, self.dtype))
+        for a in assigns:
+            self._stage(plan, a)
+            idx = self.place_index(layout, a)
+            self.be.copy_device(sp["idx"].ptr, idx.ptr, len(idx) * 8)
+            sp["graph"].launch()
+        return sp["acc"]
+
+    def _grad_plan(self, assign):
+        """The reduced tree of the value plan (same fixed buffers), its
+        forward with tape recorded once as a graph; the tape stays valid
+        across replays.  Gradients reaching a hoisted leaf continue through
+        the tape its subtree was contracted with."""
+        key = frozenset(assign.keys())
+        gp = self._grad_plans.get(key)
+        if gp is not None:
+            return gp
+        plan = self._ensure_plan(assign)
+        ein = plan["ein"]
+        out = self.be.alloc(ein.out_size(), self.dtype)
+        grads, sub_grads, gbuf, inputs_end = self._grad_buffers(plan, key)
         gp = {"ein": ein, "out": out, "grads": grads, "sub_grads": sub_grads, "gbuf": gbuf,
               "inputs_end": inputs_end, "graph": None, "tape": None, "plan": plan}
         if self.use_graph:
@@ -405,6 +502,12 @@ class DeviceExecutor:
                                           dst_ptr, 1 if accumulate else 0))
 
     def __del__(self):
+        for sp in getattr(self, "_std_plans", {}).values():
+            if sp.get("tape") is not None:
+                try:
+                    self.E.Einsum.tape_free(sp["tape"])
+                except Exception:
+                    pass
         for gp in getattr(self, "_grad_plans", {}).values():
             if gp.get("tape") is not None:
                 try:
@@ -636,8 +739,13 @@ def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device
     if on_device:
         with ctx:
             buf = torch.zeros(1 + layout.total, dtype=tdt, device=device)
-            for s in mine:
-                executor.grad_into(assigns[s], layout, buf.data_ptr(), accumulate=True)
+            if executor.use_graph:
+                acc = executor.std_sum([assigns[s] for s in mine], layout)
+                if acc is not None:
+                    executor.be.copy_device(buf.data_ptr(), acc.ptr, acc.nbytes)
+            else:
+                for s in mine:
+                    executor.grad_into(assigns[s], layout, buf.data_ptr(), accumulate=True)
             if multi:
                 _collective(dist, lambda **kw: dist.all_reduce(buf, op=dist.ReduceOp.SUM, **kw),
                             timeout_s, "slice-sum all-reduce")

@@ -140,20 +140,26 @@ class Engine:
             cshape = self.shape_of(contracted)
             oshape = self.shape_of(iy)
             am = nd["am"].astype(np.int64)
-            for o in range(len(dy)):
-                vals = {}
-                rem = o
-                for l, s in zip(iy, oshape):
-                    vals[l] = rem % s
-                    rem //= s
-                w = int(am[o])
-                for l, s in zip(contracted, cshape):
-                    vals[l] = w % s
-                    w //= s
-                pa = sum(vals[l] * st for l, st in zip(ia, _col(lt.shape)))
-                pb = sum(vals[l] * st for l, st in zip(ib, _col(rt.shape)))
-                ga[pa] += dy[o]
-                gb[pb] += dy[o]
+            # every output element o routes dy[o] to the one element of each
+            # operand that produced it; np.add.at applies the additions in
+            # order of o, as the reference's loop over output elements does
+            vals = {}
+            rem = np.arange(len(dy), dtype=np.int64)
+            for l, s in zip(iy, oshape):
+                vals[l] = rem % s
+                rem //= s
+            w = am.copy()
+            for l, s in zip(contracted, cshape):
+                vals[l] = w % s
+                w //= s
+            pa = np.zeros(len(dy), dtype=np.int64)
+            for l, st in zip(ia, _col(lt.shape)):
+                pa += vals[l] * st
+            pb = np.zeros(len(dy), dtype=np.int64)
+            for l, st in zip(ib, _col(rt.shape)):
+                pb += vals[l] * st
+            np.add.at(ga, pa, dy)
+            np.add.at(gb, pb, dy)
         else:
             d = _T(dy, iy, self.shape_of(iy))
             ga = self.contract(d, rt, ia, False)[0].buf

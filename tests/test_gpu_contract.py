@@ -384,3 +384,25 @@ def test_graph_replay_of_contractions(be):
         g.launch()
         rc, ram = orc.gemm("maxplus", a, b, m, k, n, argmax=True)
         assert bits_equal(C.to_vec(), rc) and np.array_equal(AM.to_vec(), ram)
+
+
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul", "standard"])
+@pytest.mark.parametrize("special", ["ties", "nan_inf", "normal"])
+@pytest.mark.parametrize("nout", [1, 3])
+def test_long_k_few_outputs_split_k(be, alg, special, nout):
+    """Nodes with a handful of outputs and a long contracted range (a
+    network's root dot product) split k over a CTA; the tropical combine must
+    reproduce the sequential first-k rule, NaN products included."""
+    if alg == "standard" and special == "nan_inf":
+        pytest.skip("the Standard bound is relative; NaN/inf sums are covered elsewhere")
+    sa, sb = [8, 16, 32, nout], [32, 16, 8, nout]  # contracted (0,1,2): K = 4096
+    n = int(np.prod(sa))
+    if special == "ties":
+        a, b = orc.ties(91, n), orc.ties(92, n)
+    else:
+        a, b = orc.uniform(93, n), orc.uniform(94, n)
+    if special == "nan_inf":
+        a[[5, 700, 3000]] = [np.nan, np.inf, -np.inf]
+        b[[17, 2222]] = [np.nan, -np.inf]
+    check_case(be, alg, a, sa, col(sa), [0, 1, 2, 3], b, sb, col(sb), [2, 1, 0, 3], [nout], [3],
+               argmax=alg != "standard")
