@@ -7,6 +7,7 @@
 // release threshold, so freed blocks are cached and reused without a device
 // synchronisation -- the device-side counterpart of the CPU ScratchPool
 // (src/backend/cpu/buffer_pool.rs:2-47).
+#include <map>
 #include <mutex>
 #include <set>
 #include <cstdlib>
@@ -78,11 +79,12 @@ static void resolve_pending(om_backend* be) {
 }
 
 Scratch::~Scratch() {
-  if (ptr && be) be_free(be, ptr);
+  if (ptr && be) be_free(be, be_id, ptr);
 }
 
 int Scratch::alloc(om_backend* b, size_t bytes) {
   be = b;
+  be_id = b->id;
   if (bytes == 0) bytes = 16;
   return be_alloc(b, bytes, &ptr);
 }
@@ -93,11 +95,12 @@ int Scratch::alloc(om_backend* b, size_t bytes) {
 // destructors would have run.
 static std::mutex& g_arena_mu = *new std::mutex;
 static std::set<Arena*>& g_arenas = *new std::set<Arena*>;
-static std::set<const om_backend*>& g_live = *new std::set<const om_backend*>;
+static std::map<const om_backend*, uint64_t>& g_live = *new std::map<const om_backend*, uint64_t>;
+static uint64_t g_next_backend_id = 1;
 
-static void backend_live(const om_backend* be, bool on) {
+static void backend_live(om_backend* be, bool on) {
   std::lock_guard<std::mutex> lk(g_arena_mu);
-  if (on) g_live.insert(be);
+  if (on) g_live[be] = be->id = g_next_backend_id++;
   else g_live.erase(be);
 }
 
@@ -182,7 +185,7 @@ int be_alloc(om_backend* be, size_t bytes, void** out) {
   return OM_OK;
 }
 
-void be_free(om_backend* be, void* p) {
+void be_free(om_backend* be, uint64_t id, void* p) {
   if (!p) return;
   {
     std::lock_guard<std::mutex> lk(g_arena_mu);
@@ -193,7 +196,8 @@ void be_free(om_backend* be, void* p) {
       }
     // a buffer that outlives its backend (a tape freed after
     // om_b200_destroy) goes back with the device's pool at teardown
-    if (!g_live.count(be)) return;
+    auto it = g_live.find(be);
+    if (it == g_live.end() || it->second != id) return;
   }
   cudaFreeAsync(p, be->stream);
 }

@@ -39,7 +39,8 @@ std::shared_ptr<void> dev_alloc(om_backend* be, size_t bytes, int* rc) {
   void* p = nullptr;
   *rc = be_alloc(be, bytes ? bytes : 16, &p);
   if (*rc != OM_OK) return nullptr;
-  return std::shared_ptr<void>(p, [be](void* q) { be_free(be, q); });
+  const uint64_t id = be->id;
+  return std::shared_ptr<void>(p, [be, id](void* q) { be_free(be, id, q); });
 }
 
 struct DTensor {

@@ -18,6 +18,9 @@ struct Arena;
 
 struct om_backend {
   int device = 0;
+  // process-unique id: a freed backend's address can be reused by a later
+  // one, so owners of its buffers check liveness by (address, id)
+  uint64_t id = 0;
   // while a graph is being recorded, the library's own device memory comes
   // from this arena (owned by the graph) instead of the stream-ordered pool
   om::Arena* recording = nullptr;
@@ -85,13 +88,14 @@ struct Arena {
 int be_alloc(om_backend* be, size_t bytes, void** out);
 // frees p: into the live arena that holds it, if any (a destroyed arena's
 // blocks are gone with it), else stream-ordered to the pool
-void be_free(om_backend* be, void* p);
+void be_free(om_backend* be, uint64_t id, void* p);
 void arena_register(Arena* a);
 void arena_unregister(Arena* a);
 
 // ---- scratch memory (stream-ordered, cached by the device pool) -----------
 struct Scratch {
   om_backend* be = nullptr;
+  uint64_t be_id = 0;
   void* ptr = nullptr;
   Scratch() = default;
   Scratch(const Scratch&) = delete;
