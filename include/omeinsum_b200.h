@@ -144,6 +144,18 @@ int om_b200_set_f32_mode(om_backend* be, om_f32_mode mode);
 int om_b200_scatter_index(om_backend* be, om_dtype dtype, const void* src, int64_t n,
                           const int64_t* idx, void* dst, int accumulate);
 
+/* Many strided gathers in one launch (no counterpart in the reference: the
+ * sliced network driver stages a slice's views of the sliced input tensors
+ * with it).  desc (device) holds nviews descriptors of 28 int64 words each:
+ * source pointer, destination pointer, ndim (<= 12), element count, then 12
+ * extents and 12 element strides (column-major odometer over the extents).
+ * View v of slice s starts at element offsets[s * nviews + v] (device) of its
+ * source; s is read on the device from *sel, so a graph recorded around this
+ * call serves every slice.  Destinations are contiguous.  max_numel bounds
+ * the views' element counts (it sizes the grid). */
+int om_b200_gather_views(om_backend* be, om_dtype dtype, int nviews, const int64_t* desc,
+                         const int64_t* offsets, const int32_t* sel, int64_t max_numel);
+
 /* Kernel launches issued by this thread since the last call (counter reset
  * on read); used by benchmarks to report how many device kernels ran. */
 int64_t om_b200_launch_count(void);

@@ -39,7 +39,7 @@ EXPORTS = [
     "om_b200_tropical_matmul_argmax_noalloc", "om_b200_einsum", "om_b200_einsum_backward",
     "om_b200_tape_free", "om_b200_graph_begin", "om_b200_graph_end", "om_b200_graph_launch",
     "om_b200_graph_free", "om_b200_tape_release", "om_b200_einsum_backward_linked",
-    "om_b200_set_f32_mode", "om_b200_scatter_index",
+    "om_b200_set_f32_mode", "om_b200_scatter_index", "om_b200_gather_views",
 ]
 
 
@@ -90,6 +90,7 @@ def lib():
         L.om_b200_profile_enable.argtypes = [P, I]
         L.om_b200_set_f32_mode.argtypes = [P, I]
         L.om_b200_scatter_index.argtypes = [P, I, P, I64, P, P, I]
+        L.om_b200_gather_views.argtypes = [P, I, I, P, P, P, I64]
         L.om_b200_profile_query.argtypes = [P, I, ctypes.c_char_p, SZ,
                                             ctypes.POINTER(ctypes.c_double),
                                             ctypes.POINTER(ctypes.c_int64)]

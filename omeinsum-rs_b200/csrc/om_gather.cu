@@ -540,3 +540,61 @@ extern "C" int om_b200_copy_strided(om_backend* be, om_dtype dtype, const void* 
   OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
   return launch_gather(be, dtype_size(dtype), src, ndim, shape, strides, offset, dst);
 }
+
+// ---- slice staging: many strided views in one launch -----------------------
+// Descriptor of one view, as 2 + 2 * kStageDims + 2 int64 words:
+//   [src, dst, ndim, numel, shape[kStageDims], strides[kStageDims]]
+// (pointers as integers).  The offset of view v in slice s is
+// offsets[s * nviews + v]; s is read from the device word *sel, so a
+// recorded graph serves every slice and a slice is chosen by one 4-byte
+// device copy before the replay.
+namespace om {
+namespace {
+constexpr int kStageDims = 12;
+constexpr int kStageWords = 4 + 2 * kStageDims;
+
+template <typename T>
+__global__ void gather_views_kernel(const int64_t* __restrict__ desc, int nviews,
+                                    const int64_t* __restrict__ offsets,
+                                    const int32_t* __restrict__ sel) {
+  const int v = blockIdx.y;
+  const int64_t* d = desc + (int64_t)v * kStageWords;
+  const T* src = (const T*)d[0];
+  T* dst = (T*)d[1];
+  const int nd = (int)d[2];
+  const int64_t n = d[3];
+  const int64_t off = offsets[(int64_t)(*sel) * nviews + v];
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = e, at = off;
+    for (int q = 0; q < nd; ++q) {
+      const int64_t c = rem % d[4 + q];
+      rem /= d[4 + q];
+      at += c * d[4 + kStageDims + q];
+    }
+    dst[e] = src[at];
+  }
+}
+}  // namespace
+}  // namespace om
+
+extern "C" int om_b200_gather_views(om_backend* be, om_dtype dtype, int nviews, const int64_t* desc,
+                                    const int64_t* offsets, const int32_t* sel, int64_t max_numel) {
+  using namespace om;
+  if (!be || nviews < 0 || (nviews > 0 && (!desc || !offsets || !sel)) || max_numel < 0)
+    return set_error(OM_ERR_INVALID, "om_b200_gather_views: bad argument");
+  if (nviews > 65535) return set_error(OM_ERR_INVALID, "om_b200_gather_views: more than 65535 views");
+  if (nviews == 0 || max_numel == 0) return OM_OK;
+  OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((max_numel + 255) / 256, be->num_sms * 4));
+  const dim3 grid(gx, (unsigned)nviews);
+  ProfScope prof(be, "gather_views");
+  if (dtype == OM_F64)
+    gather_views_kernel<double><<<grid, 256, 0, be->stream>>>(desc, nviews, offsets, sel);
+  else if (dtype == OM_F32 || dtype == OM_U32)
+    gather_views_kernel<float><<<grid, 256, 0, be->stream>>>(desc, nviews, offsets, sel);
+  else
+    return set_error(OM_ERR_UNSUPPORTED, "om_b200_gather_views: unknown dtype");
+  note_launch();
+  return check_cuda(cudaGetLastError(), "gather_views launch");
+}

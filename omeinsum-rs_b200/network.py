@@ -236,9 +236,85 @@ class DeviceExecutor:
         return {"ein": ein, "views": views, "tensors": tensors, "stage": stage, "out": out,
                 "graph": None}
 
+    STAGE_DIMS = 12  # per-view extent limit of om_b200_gather_views
+
+    def _stage_tables(self, plan, keys):
+        """Device tables that let one launch stage every sliced leaf of any
+        slice: a descriptor per staged view, the views' offsets for every
+        slice of these sliced labels (mixed radix over the labels in sorted
+        order, the first fastest), the selected slice id and the ids 0..n-1
+        to select from.  None when a view has too many extents."""
+        labels = sorted(keys)
+        radix = [self.sizes[l] for l in labels]
+        nsl = int(np.prod(radix)) if radix else 1
+        D = self.STAGE_DIMS
+        descs, offs, maxn = [], np.zeros((nsl, max(1, len(plan["stage"]))), np.int64), 1
+        digits = np.zeros((nsl, len(labels)), np.int64)
+        rem = np.arange(nsl)
+        for j, r in enumerate(radix):
+            digits[:, j] = rem % r
+            rem //= r
+        for v, (i, buf) in enumerate(plan["stage"]):
+            shape = [self.sizes[l] for l in self.ixs[i]]
+            st, acc = [], 1
+            for d in shape:
+                st.append(acc)
+                acc *= d
+            vs = [d for l, d in zip(self.ixs[i], shape) if l not in keys]
+            vst = [t for l, t in zip(self.ixs[i], st) if l not in keys]
+            if len(vs) > D:
+                return None
+            n = int(np.prod(vs)) if vs else 1
+            maxn = max(maxn, n)
+            descs.append([self.dev[i].ptr, buf.ptr, len(vs), n] + vs + [1] * (D - len(vs)) +
+                         vst + [0] * (D - len(vst)))
+            for j, l in enumerate(labels):
+                for l2, t in zip(self.ixs[i], st):
+                    if l2 == l:
+                        offs[:, v] += digits[:, j] * t
+        if not descs:
+            return None
+        mult, m = {}, 1
+        for l, r in zip(labels, radix):
+            mult[l] = m
+            m *= r
+        return {"desc": self.be.from_slice(np.asarray(descs, np.int64)),
+                "offs": self.be.from_slice(offs), "nviews": len(descs), "maxn": maxn,
+                "sel": self.be.from_slice(np.zeros(1, np.uint32)),
+                "ids": self.be.from_slice(np.arange(nsl, dtype=np.uint32)), "mult": mult}
+
+    def _select(self, plan, assign):
+        """Selects the slice that the next staging gather (_gather, or a graph
+        recorded around it) copies: one 4-byte device copy."""
+        if "tables" not in plan:
+            plan["tables"] = self._stage_tables(plan, frozenset(assign.keys()))
+        tb = plan["tables"]
+        if tb is None:
+            return False
+        sid = sum(assign[l] * m for l, m in tb["mult"].items())
+        self.be.copy_device(tb["sel"].ptr, tb["ids"].ptr + 4 * sid, 4)
+        return True
+
+    def _gather(self, plan):
+        """Stages the selected slice's views of every sliced leaf (one launch)."""
+        tb = plan.get("tables")
+        if tb is None:
+            return
+        om = sys.modules[type(self.be).__module__]
+        om._check(om.lib().om_b200_gather_views(
+            self.be.h, om.DTYPES[np.dtype(self.dtype)], tb["nviews"], tb["desc"].ptr,
+            tb["offs"].ptr, tb["sel"].ptr, tb["maxn"]))
+
     def _stage(self, plan, assign):
-        """Copy the slice's view of every sliced leaf into its staging buffer
-        (view shapes and strides are fixed per plan; only offsets change)."""
+        """Copy the slice's view of every sliced leaf into its staging buffer:
+        one gather launch through the device tables, or one strided copy per
+        leaf when a view has more extents than the gather takes."""
+        if self._select(plan, assign):
+            self._gather(plan)
+            return
+        self._stage_each(plan, assign)
+
+    def _stage_each(self, plan, assign):
         if "stage_views" not in plan:
             plan["stage_views"] = []
             for i, buf in plan["stage"]:
@@ -254,6 +330,14 @@ class DeviceExecutor:
         for i, buf, fixed, vs, vst in plan["stage_views"]:
             off = sum(assign[l] * t for l, t in fixed)
             self.be.copy_strided_into(self.dev[i], vs, vst, off, buf)
+
+    def _prepare(self, plan, assign):
+        """Before a graph replay: select the slice when the graph stages it
+        itself (it was recorded with the gather), else stage it here."""
+        if plan.get("tables") is not None:
+            self._select(plan, assign)
+        else:
+            self._stage_each(plan, assign)
 
     def values(self, assigns):
         """Values of several slices: each replay leaves its result in a slot
@@ -275,9 +359,12 @@ class DeviceExecutor:
         if plan is None:
             plan = self._plans[key] = self._plan(assign)
             if self.use_graph:
-                # record one slice's contraction once; every slice replays it
+                # record one slice's staging and contraction once; every
+                # slice replays it
+                self._select(plan, assign)
                 self.be.graph_begin()
                 try:
+                    self._gather(plan)
                     plan["ein"].call_views(self.be, self.alg, plan["tensors"], plan["views"],
                                            plan["out"], None)
                 finally:
@@ -285,10 +372,11 @@ class DeviceExecutor:
         return plan
 
     def _run(self, plan, assign):
-        self._stage(plan, assign)
         if plan["graph"] is not None:
+            self._prepare(plan, assign)
             plan["graph"].launch()
         else:
+            self._stage(plan, assign)
             plan["ein"].call_views(self.be, self.alg, plan["tensors"], plan["views"], plan["out"],
                                    None)
 
@@ -355,8 +443,10 @@ class DeviceExecutor:
               "acc": self.be.alloc(1 + layout.total, self.dtype),
               "grads": grads, "sub_grads": sub_grads, "gbuf": gbuf, "n": inputs_end,
               "layout": layout, "tape": None}
+        self._select(plan, assign)
         self.be.graph_begin()
         try:
+            self._gather(plan)
             sp["tape"] = ein.forward_tape_views(self.be, self.alg, plan["tensors"], plan["views"],
                                                 sp["out"])
             ein.backward_tape(sp["tape"], sp["dy"], grads)
@@ -382,7 +472,7 @@ class DeviceExecutor:
         plan = self._ensure_plan(assigns[0])
         self.be.upload_into(sp["acc"], np.zeros(1 + layout.total, self.dtype))
         for a in assigns:
-            self._stage(plan, a)
+            self._prepare(plan, a)
             idx = self.place_index(layout, a)
             self.be.copy_device(sp["idx"].ptr, idx.ptr, len(idx) * 8)
             sp["graph"].launch()
@@ -404,9 +494,10 @@ class DeviceExecutor:
         gp = {"ein": ein, "out": out, "grads": grads, "sub_grads": sub_grads, "gbuf": gbuf,
               "inputs_end": inputs_end, "graph": None, "tape": None, "plan": plan}
         if self.use_graph:
-            self._stage(plan, assign)
+            self._select(plan, assign)
             self.be.graph_begin()
             try:
+                self._gather(plan)
                 gp["tape"] = ein.forward_tape_views(self.be, self.alg, plan["tensors"],
                                                     plan["views"], out)
             finally:
@@ -422,11 +513,12 @@ class DeviceExecutor:
         gp["out"].  Returns the gradient plan."""
         gp = self._grad_plan(assign)
         plan = gp["plan"]
-        self._stage(plan, assign)
         if gp["graph"] is not None:
+            self._prepare(plan, assign)
             gp["graph"].launch()
             tape = gp["tape"]
         else:
+            self._stage(plan, assign)
             tape = gp["ein"].forward_tape_views(self.be, self.alg, plan["tensors"], plan["views"],
                                                 gp["out"])
         leaves = self._reduce(assign.keys())[0]
