@@ -580,7 +580,7 @@ def main():
     ap.add_argument("--no-check", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="leave out the network CPU baselines")
     ap.add_argument("--case", default="headline", choices=["headline", "config2", "contract", "network", "slices",
-                             "networks"],
+                             "networks", "scaling"],
                     help="profiling cases: config2 = only the config-2 permuted "
                          "contraction; contract = only warmup + steps headline calls; "
                          "network = only the sliced MIS network, with its kernel breakdown; "
@@ -628,6 +628,23 @@ def main():
                                    sorted(prof.items(), key=lambda kv: -kv[1][0])}
         print(json.dumps(net), flush=True)
         be.close()
+        return
+    if args.case == "scaling":
+        # the sliced networks alone, at N ranks (scaling runs of those objects)
+        import torch
+        om = load_pkg()
+        torch.cuda.set_device(local_rank)
+        if world > 1:
+            torch.distributed.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
+        be = om.B200(local_rank)
+        out = {"network": run_network(be, om, world, rank, local_rank, args),
+               "network_8_slices": run_network(be, om, world, rank, local_rank, args, nsliced=3),
+               "config5": run_config5(be, om, world, rank, local_rank)}
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        be.close()
+        if world > 1:
+            torch.distributed.destroy_process_group()
         return
     if args.case == "slices" and world == 1:
         import importlib

@@ -202,6 +202,24 @@ int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, int ntensors,
                    int nnodes, const int32_t* children, const int32_t* node_iy_off,
                    const int32_t* node_iy, void* out, om_tape** tape_out);
 
+/* om_b200_einsum with a tape of values only (tropical algebras): every
+ * intermediate is kept, but no node computes its argmax.  The backward
+ * (om_b200_einsum_backward / _linked, outputs of at most 4096 elements)
+ * then finds the argmax of just the elements the gradient visits, from the
+ * children's values, with the same rule as the forward (generic_gemm_with_argmax,
+ * src/backend/cpu/mod.rs:889-920, and execute_unary_with_argmax,
+ * src/einsum/engine.rs:841-926), so the gradient is the one the argmax tape
+ * gives.  No counterpart in the reference: it lets a caller contract many
+ * candidates (the slices of a sliced network) at value cost and take the
+ * gradient of the winner only. */
+int om_b200_einsum_tape_values(om_backend* be, om_algebra alg, om_dtype dtype, int ntensors,
+                               const void* const* tensors, const int32_t* ndims,
+                               const int64_t* shapes, const int64_t* strides, const int32_t* ixs,
+                               int niy, const int32_t* iy, int nsizes, const int32_t* size_labels,
+                               const int64_t* size_values, int nnodes, const int32_t* children,
+                               const int32_t* node_iy_off, const int32_t* node_iy, void* out,
+                               om_tape** tape_out);
+
 /* GradientTape::backward (backward.rs:498-506, 678-728): given dy (shaped
  * like the output, contiguous), writes the gradient of every input tensor t,
  * contiguous column-major in the input's shape, to grads[t]. */

@@ -102,9 +102,16 @@ struct SpNode {
   int off;      // binary: first record in SpMode data (nc output modes, then nk contracted)
   const uint32_t* argmax;
   void* grad;   // leaf
+  // tapes kept without argmax (om_b200_einsum_tape_values): the argmax of a
+  // visited element is found from the children's values instead
+  int lazy;
+  const void* xa;  // binary: left child's values; unary: the input's values
+  const void* xb;  // binary: right child's values
+  int64_t aux;     // unary: first word of its descriptor in the aux array
 };
 struct SpMode {
   int64_t ext, sa, sb;  // extent; element stride in the left / right child (0 if absent)
+  int64_t da, db;       // the same in the children's memory (their value strides)
 };
 
 template <typename T>
@@ -152,6 +159,188 @@ __global__ void __launch_bounds__(512) sparse_backward_kernel(const SpNode* __re
   }
 }
 
+// The same walk over tapes kept without argmax: a warp per entry.  The
+// argmax of a binary node's entry is recomputed from the children's values
+// with the rule of generic_gemm_with_argmax (start at zero(), replace on
+// strict improvement, so the first k reaching the maximum wins); the lanes
+// split k and merge (better value, then smaller k).  A NaN product breaks
+// that merge (the sequential rule lets a NaN replace and be replaced), so a
+// node entry that meets one is rescanned sequentially by lane 0.  A unary
+// node's entry follows execute_unary_with_argmax (first inner element, then
+// strict improvement; the winner's column-major position in the input).
+// Unary descriptor words in aux: nx, ny, ninner, nslots, xslot[nx],
+// xstride[nx], xlogical[nx], yslot[ny], ysize[ny], islot[ninner],
+// isize[ninner].
+template <typename T, int ALG>
+__device__ __forceinline__ void lazy_better(T v, int64_t k, T& best, int64_t& bk) {
+  if (Semi<ALG, T>::better(v, best) || (v == best && k < bk)) {
+    best = v;
+    bk = k;
+  }
+}
+
+template <typename T, int ALG>
+__global__ void __launch_bounds__(1024) sparse_backward_lazy_kernel(
+    const SpNode* __restrict__ nodes, const SpMode* __restrict__ modes,
+    const int64_t* __restrict__ aux, const int* __restrict__ level_start, int nlevels, int root,
+    int64_t* lists, const T* __restrict__ val, int64_t n) {
+  using S = Semi<ALG, T>;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int64_t e = threadIdx.x; e < n; e += blockDim.x) lists[(int64_t)root * n + e] = e;
+  __syncthreads();
+  for (int L = 0; L < nlevels; ++L) {
+    const int first = level_start[L];
+    const int64_t items = (int64_t)(level_start[L + 1] - first) * n;
+    for (int64_t it = warp; it < items; it += nwarps) {
+      const int id = first + (int)(it / n);
+      const int64_t e = it % n;
+      const SpNode nd = nodes[id];
+      const int64_t o = lists[(int64_t)id * n + e];
+      if (nd.kind == 0) {
+        if (lane == 0) {
+          const T v = val[e];
+          if (v != T(0)) atomicAdd((T*)nd.grad + o, v);
+        }
+      } else if (nd.kind == 1 && !nd.lazy) {
+        if (lane == 0) lists[(int64_t)nd.child0 * n + e] = nd.argmax ? (int64_t)nd.argmax[o] : o;
+      } else if (nd.kind == 1) {
+        const int64_t* d = aux + nd.aux;
+        const int nx = (int)d[0], ny = (int)d[1], ni = (int)d[2], ns = (int)d[3];
+        const int64_t *xslot = d + 4, *xstride = xslot + nx, *xlog = xstride + nx;
+        const int64_t *yslot = xlog + nx, *ysize = yslot + ny, *islot = ysize + ny,
+                      *isize = islot + ni;
+        int64_t v_[OM_MAX_DIMS];
+        bool set[OM_MAX_DIMS];
+        for (int q = 0; q < ns; ++q) set[q] = false;
+        int64_t rem = o;
+        bool skip = false;
+        for (int q = 0; q < ny; ++q) {
+          const int64_t c = rem % ysize[q];
+          rem /= ysize[q];
+          const int sl = (int)yslot[q];
+          if (set[sl] && v_[sl] != c) skip = true;
+          set[sl] = true;
+          v_[sl] = c;
+        }
+        int64_t inner = 1;
+        for (int q = 0; q < ni; ++q) inner *= isize[q];
+        const T* X = (const T*)nd.xa;
+        T best = T(0);
+        int64_t bk = INT64_MAX, bpos = 0;
+        bool first_nan = false;
+        if (!skip) {
+          for (int64_t in = lane; in < inner; in += 32) {
+            int64_t r2 = in;
+            for (int q = 0; q < ni; ++q) {
+              v_[islot[q]] = r2 % isize[q];
+              r2 /= isize[q];
+            }
+            int64_t off = 0, lpos = 0;
+            for (int q = 0; q < nx; ++q) {
+              off += v_[xslot[q]] * xstride[q];
+              lpos += v_[xslot[q]] * xlog[q];
+            }
+            const T x = X[off];
+            if (in == 0) first_nan = x != x;
+            if (x == x && (bk == INT64_MAX || S::better(x, best) || (x == best && in < bk))) {
+              best = x;
+              bk = in;
+              bpos = lpos;
+            }
+          }
+        }
+        // merge: better value, then earlier inner position; a NaN first
+        // element keeps position 0 (nothing is strictly better than NaN)
+        for (int sh = 16; sh; sh >>= 1) {
+          const T ob = __shfl_xor_sync(0xffffffffu, best, sh);
+          const int64_t ok = __shfl_xor_sync(0xffffffffu, bk, sh);
+          const int64_t op = __shfl_xor_sync(0xffffffffu, bpos, sh);
+          if (ok != INT64_MAX && (bk == INT64_MAX || S::better(ob, best) || (ob == best && ok < bk))) {
+            best = ob;
+            bk = ok;
+            bpos = op;
+          }
+        }
+        first_nan = __shfl_sync(0xffffffffu, first_nan, 0);
+        if (lane == 0) lists[(int64_t)nd.child0 * n + e] = (skip || first_nan || bk == INT64_MAX) ? 0 : bpos;
+      } else {
+        const SpMode* m = modes + nd.off;
+        int64_t pa = 0, pb = 0, qa = 0, qb = 0, rem = o;
+        for (int k = 0; k < nd.nc; ++k) {
+          const int64_t c = rem % m[k].ext;
+          rem /= m[k].ext;
+          pa += c * m[k].sa;
+          pb += c * m[k].sb;
+          qa += c * m[k].da;
+          qb += c * m[k].db;
+        }
+        int64_t w = 0;
+        if (nd.argmax) {
+          w = nd.argmax[o];
+        } else {
+          int64_t K = 1;
+          for (int k = nd.nc; k < nd.nc + nd.nk; ++k) K *= m[k].ext;
+          const T* A = (const T*)nd.xa;
+          const T* B = (const T*)nd.xb;
+          auto prod = [&](int64_t kk) {
+            int64_t ra = qa, rb = qb;
+            for (int k = nd.nc; k < nd.nc + nd.nk; ++k) {
+              const int64_t c = kk % m[k].ext;
+              kk /= m[k].ext;
+              ra += c * m[k].da;
+              rb += c * m[k].db;
+            }
+            return S::mul(A[ra], B[rb]);
+          };
+          T best = S::zero();
+          int64_t bk = INT64_MAX;
+          bool nan = false;
+          for (int64_t kk = lane; kk < K; kk += 32) {
+            const T p = prod(kk);
+            nan |= p != p;
+            if (S::better(p, best)) {
+              best = p;
+              bk = kk;
+            }
+          }
+          for (int sh = 16; sh; sh >>= 1) {
+            const T ob = __shfl_xor_sync(0xffffffffu, best, sh);
+            const int64_t ok = __shfl_xor_sync(0xffffffffu, bk, sh);
+            lazy_better<T, ALG>(ob, ok, best, bk);
+          }
+          w = bk == INT64_MAX ? 0 : bk;
+          if (__any_sync(0xffffffffu, nan)) {  // the sequential rule, as in the forward
+            if (lane == 0) {
+              T acc = S::zero();
+              int64_t idx = 0;
+              for (int64_t kk = 0; kk < K; ++kk) {
+                const T p = prod(kk);
+                if (!S::keep(acc, p)) {
+                  acc = p;
+                  idx = kk;
+                }
+              }
+              w = idx;
+            }
+          }
+          w = __shfl_sync(0xffffffffu, w, 0);
+        }
+        if (lane == 0) {
+          for (int k = nd.nc; k < nd.nc + nd.nk; ++k) {
+            const int64_t c = w % m[k].ext;
+            w /= m[k].ext;
+            pa += c * m[k].sa;
+            pb += c * m[k].sb;
+          }
+          lists[(int64_t)nd.child0 * n + e] = pa;
+          lists[(int64_t)nd.child1 * n + e] = pb;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 template <typename T>
 __global__ void zero_many_kernel(T* const* ptrs, const int64_t* sizes, int count) {
   for (int q = blockIdx.x; q < count; q += gridDim.x)
@@ -174,6 +363,7 @@ struct Engine {
   std::vector<std::vector<int64_t>> input_shapes;
   int root = -1;
   bool keep;  // tape mode (argmax for tropical)
+  bool lazy = false;  // tropical tape kept without argmax (values only)
 
   int64_t extent(int32_t l) const {
     auto it = sizes.find(l);
@@ -303,7 +493,7 @@ struct Engine {
     n.in_ix = nodes[child].content.ix;
     n.out_ix = oix;
     n.child0 = child;
-    OM_TRY(unary(nodes[child].content, oix, keep && tropical, n.content, n.argmax));
+    OM_TRY(unary(nodes[child].content, oix, keep && tropical && !lazy, n.content, n.argmax));
     n.am = (const uint32_t*)n.argmax.get();
     nodes.push_back(std::move(n));
     *out_node = (int)nodes.size() - 1;
@@ -318,6 +508,44 @@ struct Engine {
       return OM_OK;
     }
     return push_unary(node, nix, out_node);
+  }
+
+  // descriptor words of a unary node for the lazy backward walk (the same
+  // label analysis as launch_unary: slots per distinct label, inner labels =
+  // labels of x absent from the output, first occurrence order)
+  static int unary_aux(const DTensor& x, const std::vector<int32_t>& oix,
+                       const std::vector<int64_t>& osize, std::vector<int64_t>& aux) {
+    std::vector<int32_t> slots;
+    auto slot_of = [&](int32_t l) -> int64_t {
+      for (size_t i = 0; i < slots.size(); ++i)
+        if (slots[i] == l) return (int64_t)i;
+      slots.push_back(l);
+      return (int64_t)slots.size() - 1;
+    };
+    const int nx = (int)x.ix.size(), ny = (int)oix.size();
+    std::vector<int64_t> xs, xst, xl, ys, yz, is, iz;
+    int64_t lg = 1;
+    for (int q = 0; q < nx; ++q) {
+      xs.push_back(slot_of(x.ix[q]));
+      xst.push_back(x.strides[q]);
+      xl.push_back(lg);
+      lg *= x.shape[q];
+    }
+    for (int q = 0; q < ny; ++q) {
+      ys.push_back(slot_of(oix[q]));
+      yz.push_back(osize[q]);
+    }
+    for (int q = 0; q < nx; ++q) {
+      const bool in_y = std::find(oix.begin(), oix.end(), x.ix[q]) != oix.end();
+      const bool seen = std::find(is.begin(), is.end(), xs[q]) != is.end();
+      if (in_y || seen) continue;
+      is.push_back(xs[q]);
+      iz.push_back(x.shape[q]);
+    }
+    if ((int)slots.size() > OM_MAX_DIMS) return set_error(OM_ERR_INVALID, "lazy unary: too many labels");
+    for (int64_t w : {(int64_t)nx, (int64_t)ny, (int64_t)is.size(), (int64_t)slots.size()}) aux.push_back(w);
+    for (auto* v : {&xs, &xst, &xl, &ys, &yz, &is, &iz}) aux.insert(aux.end(), v->begin(), v->end());
+    return OM_OK;
   }
 
   int backprop(int idx, const DTensor& dy, void* const* grads);
@@ -373,6 +601,8 @@ int Engine::backprop_sparse_linked(const void* dy, const std::vector<const Engin
     level_start.pop_back();
   std::vector<SpNode> recs(order.size());
   std::vector<SpMode> modes;
+  std::vector<int64_t> aux;
+  bool any_lazy = false;
   std::vector<void*> zptr;
   std::vector<int64_t> zsize;
   for (size_t q = 0; q < order.size(); ++q) {
@@ -395,6 +625,14 @@ int Engine::backprop_sparse_linked(const void* dy, const std::vector<const Engin
       r.kind = 1;
       r.child0 = slot[t.child0];
       r.argmax = t.am;
+      if (!t.am && engines[k]->lazy) {
+        r.lazy = 1;
+        any_lazy = true;
+        const DTensor& x = enodes[t.child0].content;
+        r.xa = x.ptr;
+        r.aux = (int64_t)aux.size();
+        OM_TRY(unary_aux(x, t.out_ix, t.content.shape, aux));
+      }
     } else {
       r.kind = 2;
       r.child0 = slot[t.child0];
@@ -413,9 +651,22 @@ int Engine::backprop_sparse_linked(const void* dy, const std::vector<const Engin
         return 0;
       };
       const DTensor& c = t.content;
+      // element strides of a label in a child's memory (0 if absent)
+      auto data_in = [](const DTensor& x, int32_t lab) -> int64_t {
+        for (size_t i = 0; i < x.ix.size(); ++i)
+          if (x.ix[i] == lab) return x.strides[i];
+        return 0;
+      };
+      if (!t.am && engines[k]->lazy) {
+        r.lazy = 1;
+        any_lazy = true;
+        r.xa = l.ptr;
+        r.xb = rr.ptr;
+      }
       for (size_t k = 0; k < t.out_ix.size(); ++k)
         modes.push_back({c.shape[k], stride_in(t.left_ix, l.shape, t.out_ix[k]),
-                         stride_in(t.right_ix, rr.shape, t.out_ix[k])});
+                         stride_in(t.right_ix, rr.shape, t.out_ix[k]), data_in(l, t.out_ix[k]),
+                         data_in(rr, t.out_ix[k])});
       r.nc = (int)t.out_ix.size();
       // contracted labels in left_ix order: the argmax's column-major digits
       for (size_t k = 0; k < t.left_ix.size(); ++k) {
@@ -424,7 +675,7 @@ int Engine::backprop_sparse_linked(const void* dy, const std::vector<const Engin
         const bool in_c = std::find(t.out_ix.begin(), t.out_ix.end(), lab) != t.out_ix.end();
         if (in_r && !in_c) {
           modes.push_back({l.shape[k], stride_in(t.left_ix, l.shape, lab),
-                           stride_in(t.right_ix, rr.shape, lab)});
+                           stride_in(t.right_ix, rr.shape, lab), data_in(l, lab), data_in(rr, lab)});
           r.nk++;
         }
       }
@@ -433,21 +684,25 @@ int Engine::backprop_sparse_linked(const void* dy, const std::vector<const Engin
   }
   int rc;
   const size_t b_nodes = sizeof(SpNode) * recs.size(), b_modes = sizeof(SpMode) * modes.size();
+  const size_t b_aux = 8 * aux.size();
   const size_t b_levels = sizeof(int) * level_start.size(), b_lists = 8 * order.size() * (size_t)n;
   const size_t b_z = (sizeof(void*) + 8) * zptr.size();
-  auto buf = dev_alloc(be, b_nodes + b_modes + b_levels + b_z + b_lists + 64, &rc);
+  auto buf = dev_alloc(be, b_nodes + b_modes + b_aux + b_levels + b_z + b_lists + 64, &rc);
   OM_TRY(rc);
   char* base = (char*)buf.get();
   SpNode* d_nodes = (SpNode*)base;
   SpMode* d_modes = (SpMode*)(base + b_nodes);
-  int* d_levels = (int*)(base + b_nodes + b_modes);
-  void** d_zptr = (void**)(((uintptr_t)(base + b_nodes + b_modes + b_levels) + 15) & ~(uintptr_t)15);
+  int64_t* d_aux = (int64_t*)(base + b_nodes + b_modes);
+  int* d_levels = (int*)(base + b_nodes + b_modes + b_aux);
+  const size_t b_head = b_nodes + b_modes + b_aux + b_levels;
+  void** d_zptr = (void**)(((uintptr_t)(base + b_head) + 15) & ~(uintptr_t)15);
   int64_t* d_zsize = (int64_t*)(d_zptr + zptr.size());
   int64_t* d_lists = (int64_t*)(((uintptr_t)(d_zsize + zsize.size()) + 15) & ~(uintptr_t)15);
-  std::vector<char> host(b_nodes + b_modes + b_levels);
+  std::vector<char> host(b_head);
   memcpy(host.data(), recs.data(), b_nodes);
   if (b_modes) memcpy(host.data() + b_nodes, modes.data(), b_modes);
-  memcpy(host.data() + b_nodes + b_modes, level_start.data(), b_levels);
+  if (b_aux) memcpy(host.data() + b_nodes + b_modes, aux.data(), b_aux);
+  memcpy(host.data() + b_nodes + b_modes + b_aux, level_start.data(), b_levels);
   OM_CUDA(cudaMemcpyAsync(base, host.data(), host.size(), cudaMemcpyHostToDevice, be->stream),
           "sparse backward upload");
   if (!zptr.empty()) {
@@ -462,21 +717,38 @@ int Engine::backprop_sparse_linked(const void* dy, const std::vector<const Engin
   OM_TRY(rc);
   OM_CUDA(cudaMemcpyAsync(val.get(), dy, es * (size_t)n, cudaMemcpyDeviceToDevice, be->stream),
           "grad copy");
-  ProfScope prof(be, "sparse_backward");
+  ProfScope prof(be, any_lazy ? "sparse_backward_lazy" : "sparse_backward");
   const int nz = (int)zptr.size();
+  const int nlev = (int)level_start.size() - 1;
   if (dt == OM_F32) {
     if (nz) zero_many_kernel<float><<<std::min(nz, be->num_sms * 4), 256, 0, be->stream>>>(
         (float* const*)d_zptr, d_zsize, nz);
-    sparse_backward_kernel<float><<<1, 512, 0, be->stream>>>(
-        d_nodes, d_modes, d_levels, (int)level_start.size() - 1, 0, d_lists,
-        (const float*)val.get(), n);
   } else {
     if (nz) zero_many_kernel<double><<<std::min(nz, be->num_sms * 4), 256, 0, be->stream>>>(
         (double* const*)d_zptr, d_zsize, nz);
-    sparse_backward_kernel<double><<<1, 512, 0, be->stream>>>(
-        d_nodes, d_modes, d_levels, (int)level_start.size() - 1, 0, d_lists,
-        (const double*)val.get(), n);
   }
+#define OM_LAZY(T, A)                                                                     \
+  sparse_backward_lazy_kernel<T, A><<<1, 1024, 0, be->stream>>>(d_nodes, d_modes, d_aux, d_levels, \
+                                                               nlev, 0, d_lists,             \
+                                                               (const T*)val.get(), n)
+  if (any_lazy) {
+    if (dt == OM_F32) {
+      if (alg == OM_MAXPLUS) OM_LAZY(float, OM_MAXPLUS);
+      else if (alg == OM_MINPLUS) OM_LAZY(float, OM_MINPLUS);
+      else OM_LAZY(float, OM_MAXMUL);
+    } else {
+      if (alg == OM_MAXPLUS) OM_LAZY(double, OM_MAXPLUS);
+      else if (alg == OM_MINPLUS) OM_LAZY(double, OM_MINPLUS);
+      else OM_LAZY(double, OM_MAXMUL);
+    }
+  } else if (dt == OM_F32) {
+    sparse_backward_kernel<float><<<1, 512, 0, be->stream>>>(d_nodes, d_modes, d_levels, nlev, 0,
+                                                             d_lists, (const float*)val.get(), n);
+  } else {
+    sparse_backward_kernel<double><<<1, 512, 0, be->stream>>>(d_nodes, d_modes, d_levels, nlev, 0,
+                                                              d_lists, (const double*)val.get(), n);
+  }
+#undef OM_LAZY
   note_launch(nz ? 2 : 1);
   return check_cuda(cudaGetLastError(), "sparse backward launch");
 }
@@ -550,13 +822,12 @@ struct om_tape {
 
 using namespace om;
 
-extern "C" int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, int ntensors,
-                              const void* const* tensors, const int32_t* ndims,
-                              const int64_t* shapes, const int64_t* strides, const int32_t* ixs,
-                              int niy, const int32_t* iy, int nsizes, const int32_t* size_labels,
-                              const int64_t* size_values, int nnodes, const int32_t* children,
-                              const int32_t* node_iy_off, const int32_t* node_iy, void* out,
-                              om_tape** tape_out) {
+static int einsum_impl(om_backend* be, om_algebra alg, om_dtype dtype, int ntensors,
+                       const void* const* tensors, const int32_t* ndims, const int64_t* shapes,
+                       const int64_t* strides, const int32_t* ixs, int niy, const int32_t* iy,
+                       int nsizes, const int32_t* size_labels, const int64_t* size_values,
+                       int nnodes, const int32_t* children, const int32_t* node_iy_off,
+                       const int32_t* node_iy, void* out, om_tape** tape_out, bool lazy) {
   if (!be || !tensors || !ndims || !out || ntensors < 1 || niy < 0 || nnodes < 0 ||
       (nnodes > 0 && (!children || !node_iy_off)))
     return set_error(OM_ERR_INVALID, "om_b200_einsum: bad argument");
@@ -575,6 +846,7 @@ extern "C" int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, in
   E.es = dtype_size(dtype);
   E.tropical = alg != OM_STANDARD;
   E.keep = tape_out != nullptr;
+  E.lazy = lazy && E.tropical;
   for (int q = 0; q < nsizes; ++q) E.sizes[size_labels[q]] = size_values[q];
   std::unique_ptr<om_tape> guard(tape);
 
@@ -629,7 +901,7 @@ extern "C" int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, in
       n.right_ix = E.nodes[r].content.ix;
       n.out_ix = E.node_order(E.nodes[l].content, E.nodes[r].content, niy_);
       OM_TRY(E.contract(E.nodes[l].content, n.left_ix, E.nodes[r].content, n.right_ix, n.out_ix,
-                        E.keep && E.tropical, n.content, n.argmax));
+                        E.keep && E.tropical && !E.lazy, n.content, n.argmax));
       n.am = (const uint32_t*)n.argmax.get();
       E.nodes.push_back(std::move(n));
       node_of[i] = (int)E.nodes.size() - 1;
@@ -647,6 +919,35 @@ extern "C" int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, in
   return OM_OK;
 }
 
+extern "C" int om_b200_einsum(om_backend* be, om_algebra alg, om_dtype dtype, int ntensors,
+                              const void* const* tensors, const int32_t* ndims,
+                              const int64_t* shapes, const int64_t* strides, const int32_t* ixs,
+                              int niy, const int32_t* iy, int nsizes, const int32_t* size_labels,
+                              const int64_t* size_values, int nnodes, const int32_t* children,
+                              const int32_t* node_iy_off, const int32_t* node_iy, void* out,
+                              om_tape** tape_out) {
+  return einsum_impl(be, alg, dtype, ntensors, tensors, ndims, shapes, strides, ixs, niy, iy,
+                     nsizes, size_labels, size_values, nnodes, children, node_iy_off, node_iy, out,
+                     tape_out, false);
+}
+
+extern "C" int om_b200_einsum_tape_values(om_backend* be, om_algebra alg, om_dtype dtype,
+                                          int ntensors, const void* const* tensors,
+                                          const int32_t* ndims, const int64_t* shapes,
+                                          const int64_t* strides, const int32_t* ixs, int niy,
+                                          const int32_t* iy, int nsizes,
+                                          const int32_t* size_labels, const int64_t* size_values,
+                                          int nnodes, const int32_t* children,
+                                          const int32_t* node_iy_off, const int32_t* node_iy,
+                                          void* out, om_tape** tape_out) {
+  if (!tape_out) return set_error(OM_ERR_INVALID, "om_b200_einsum_tape_values: tape_out is null");
+  if (alg == OM_STANDARD)
+    return set_error(OM_ERR_UNSUPPORTED, "om_b200_einsum_tape_values: tropical algebras only");
+  return einsum_impl(be, alg, dtype, ntensors, tensors, ndims, shapes, strides, ixs, niy, iy,
+                     nsizes, size_labels, size_values, nnodes, children, node_iy_off, node_iy, out,
+                     tape_out, true);
+}
+
 extern "C" int om_b200_einsum_backward(om_tape* tape, const void* dy, void* const* grads) {
   if (!tape || !dy || !grads) return set_error(OM_ERR_INVALID, "om_b200_einsum_backward: null argument");
   Engine& E = tape->eng;
@@ -656,6 +957,9 @@ extern "C" int om_b200_einsum_backward(om_tape* tape, const void* dy, void* cons
   d.ptr = dy;
   const int64_t n = d.numel();
   if (E.tropical && n <= kSparseGradMax) return E.backprop_sparse(dy, grads);
+  if (E.lazy)
+    return set_error(OM_ERR_UNSUPPORTED, "om_b200_einsum_backward: a values-only tape needs an "
+                                         "output of at most 4096 elements");
   return E.backprop(E.root, d, grads);
 }
 

@@ -26,6 +26,7 @@ def _bind():
         P, I = ctypes.c_void_p, ctypes.c_int
         L.om_b200_einsum.argtypes = [P, I, I, I, P, P, P, P, P, I, P, I, P, P, I, P, P, P, P,
                                      ctypes.POINTER(P)]
+        L.om_b200_einsum_tape_values.argtypes = L.om_b200_einsum.argtypes
         L.om_b200_einsum_backward.argtypes = [P, P, P]
         L.om_b200_tape_free.argtypes = [P]
         L.om_b200_tape_release.argtypes = [P]
@@ -173,9 +174,11 @@ class Einsum:
             return [], []
         return encode_tree(self.tree, self.ixs, self.iy)
 
-    def _call(self, be: B200, alg, tensors, out, tape, views=None):
+    def _call(self, be: B200, alg, tensors, out, tape, views=None, values_only=False):
         """views (optional): per tensor (element offset, shape, strides,
-        labels) of a strided view into the tensor's storage."""
+        labels) of a strided view into the tensor's storage.  values_only:
+        keep a tropical tape of values without argmax
+        (om_b200_einsum_tape_values)."""
         L = _bind()
         children, node_iys = self.encoded()
         dtype = tensors[0].dtype
@@ -194,10 +197,10 @@ class Einsum:
         ch = _i32(children)
         off = _i32(np.cumsum([0] + [len(x) for x in node_iys]))
         niy = _i32([l for x in node_iys for l in x])
-        _check(L.om_b200_einsum(be.h, _alg(alg), DTYPES[dtype], len(tensors), ptrs, _p(nd),
-                                _p(shapes), _p(strides), _p(ixs), len(iy), _p(iy), len(sl),
-                                _p(sl), _p(sv), len(node_iys), _p(ch), _p(off), _p(niy),
-                                out.ptr, tape))
+        fn = L.om_b200_einsum_tape_values if values_only else L.om_b200_einsum
+        _check(fn(be.h, _alg(alg), DTYPES[dtype], len(tensors), ptrs, _p(nd), _p(shapes),
+                  _p(strides), _p(ixs), len(iy), _p(iy), len(sl), _p(sl), _p(sv), len(node_iys),
+                  _p(ch), _p(off), _p(niy), out.ptr, tape))
 
     def out_size(self):
         return int(np.prod([self.size_dict[l] for l in self.iy])) if self.iy else 1
@@ -218,6 +221,16 @@ class Einsum:
         and stays valid across replays."""
         tape = ctypes.c_void_p()
         self._call(be, alg, tensors, out, ctypes.byref(tape), views)
+        return tape
+
+    def forward_values_tape_views(self, be: B200, alg, tensors, views, out) -> ctypes.c_void_p:
+        """Tropical forward that keeps every intermediate but computes no
+        argmax; backward_tape / backward_tape_linked then find the argmax of
+        just the elements the gradient visits (outputs of at most 4096
+        elements).  Costs what a plain forward costs, plus the memory of the
+        intermediates."""
+        tape = ctypes.c_void_p()
+        self._call(be, alg, tensors, out, ctypes.byref(tape), views, values_only=True)
         return tape
 
     @staticmethod
@@ -262,13 +275,15 @@ class Einsum:
             _bind().om_b200_tape_free(tape)
         return out, grads
 
-    def cost_and_gradient(self, be: B200, alg, tensors, dy=None):
+    def cost_and_gradient(self, be: B200, alg, tensors, dy=None, values_only=False):
         """cost_and_gradient (backward.rs:769-799).  dy defaults to the
         algebra's one() as in the reference (0 for MaxPlus/MinPlus, so pass
-        dy = [1] to recover a tropical configuration)."""
+        dy = [1] to recover a tropical configuration).  values_only: tropical
+        forward without argmax, the backward finding the argmax of the
+        elements it visits (same gradient)."""
         out = be.alloc(self.out_size(), tensors[0].dtype)
         tape = ctypes.c_void_p()
-        self._call(be, alg, tensors, out, ctypes.byref(tape))
+        self._call(be, alg, tensors, out, ctypes.byref(tape), values_only=values_only)
         try:
             if dy is None:
                 one = 1.0 if _alg(alg) in (0, 3) else 0.0

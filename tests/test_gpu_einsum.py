@@ -130,3 +130,68 @@ def test_mis_150_config3(env):
     sel = [int(x.to_vec()[1] > 0) for x in g[:150]]
     assert sum(sel) == int(val)
     assert all(not (sel[u] and sel[v]) for u, v in edges)
+
+
+# ---- values-only tapes: the backward recomputes the argmax it needs ------
+def both_tapes(E, be, alg, ixs, iy, sizes, ts, dy, tree=None):
+    ein = E.Einsum(ixs, iy, sizes)
+    if tree is not None:
+        ein.set_contraction_tree(tree)
+    else:
+        ein.optimize_greedy()
+    dev = [be.from_slice(t) for t in ts]
+    c1, g1 = ein.cost_and_gradient(be, alg, dev, dy=dy)
+    c2, g2 = ein.cost_and_gradient(be, alg, dev, dy=dy, values_only=True)
+    return (c1.to_vec(), [x.to_vec() for x in g1]), (c2.to_vec(), [x.to_vec() for x in g2])
+
+
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul"])
+def test_values_only_tape_normalisation_cases(env, alg):
+    om, E, be = env
+    rng = np.random.default_rng(12)
+    ixs = [[0, 0, 1, 5], [1, 2, 6], [2, 3], [3, 4]]
+    iy = [4, 0]
+    sizes = {0: 3, 1: 4, 2: 2, 3: 5, 4: 3, 5: 2, 6: 3}
+    ts = [np.abs(rng.standard_normal(int(np.prod([sizes[l] for l in ix])))).astype(np.float64)
+          for ix in ixs]
+    (c1, g1), (c2, g2) = both_tapes(E, be, alg, ixs, iy, sizes, ts, np.arange(1.0, 10.0))
+    np.testing.assert_array_equal(c1, c2)
+    for x, y in zip(g1, g2):
+        np.testing.assert_array_equal(x, y)
+
+
+@pytest.mark.parametrize("kind", ["ties", "specials"])
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul"])
+def test_values_only_tape_ties_and_special_values(env, alg, kind):
+    # integer-valued inputs (many equal maxima: first index must win) and
+    # inputs with NaN / +-inf / -0 (the sequential rule decides)
+    om, E, be = env
+    rng = np.random.default_rng(13)
+    ixs = [[0, 1], [1, 2, 3], [3, 4], [4, 0, 5], [5]]
+    iy = [2]
+    sizes = {0: 4, 1: 40, 2: 3, 3: 50, 4: 6, 5: 70}
+    ts = []
+    for ix in ixs:
+        n = int(np.prod([sizes[l] for l in ix]))
+        x = rng.integers(-2, 3, n).astype(np.float32)
+        if kind == "specials":
+            pick = rng.random(n)
+            x[pick < 0.02] = np.nan
+            x[(pick >= 0.02) & (pick < 0.05)] = -np.inf
+            x[(pick >= 0.05) & (pick < 0.07)] = np.inf
+            x[(pick >= 0.07) & (pick < 0.1)] = -0.0
+        ts.append(x)
+    (c1, g1), (c2, g2) = both_tapes(E, be, alg, ixs, iy, sizes, ts, np.ones(3, np.float32))
+    np.testing.assert_array_equal(c1.view(np.uint32), c2.view(np.uint32))
+    for x, y in zip(g1, g2):
+        np.testing.assert_array_equal(x, y)
+
+
+@pytest.mark.parametrize("n,seed", [(20, 2), (60, 7)])
+def test_values_only_tape_mis(env, n, seed):
+    om, E, be = env
+    ixs, iy, sizes, ts, edges = E.mis_network(n, seed)
+    (c1, g1), (c2, g2) = both_tapes(E, be, "maxplus", ixs, iy, sizes, ts, [1.0])
+    np.testing.assert_array_equal(c1, c2)
+    for x, y in zip(g1, g2):
+        np.testing.assert_array_equal(x, y)
