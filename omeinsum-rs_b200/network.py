@@ -545,6 +545,116 @@ class DeviceExecutor:
             self.E.Einsum.backward_tape(sub_tape, gp["grads"][j], sg)
         return gp
 
+    N_VALUE_SLOTS = 3
+
+    def _value_slots(self, assign):
+        """Tropical slices at value cost with the best one kept: three
+        recorded graphs, each with its own staging buffers, running a slice's
+        forward with a values-only tape (every intermediate kept, no argmax).
+        One slot holds the best slice so far, one the slice being judged, one
+        the slice running, so no replay overwrites the best slice's values."""
+        key = frozenset(assign.keys())
+        slots = self.__dict__.setdefault("_vslots", {}).get(key)
+        if slots is not None:
+            return slots
+        slots = []
+        for _ in range(self.N_VALUE_SLOTS):
+            plan = self._plan(assign)  # fresh staging buffers and output
+            self._select(plan, assign)
+            self.be.graph_begin()
+            try:
+                self._gather(plan)
+                plan["tape"] = plan["ein"].forward_values_tape_views(
+                    self.be, self.alg, plan["tensors"], plan["views"], plan["out"])
+            finally:
+                plan["graph"] = self.be.graph_end()
+            slots.append(plan)
+        self._vslots[key] = slots
+        return slots
+
+    def best_of(self, assigns, minimize):
+        """Runs the slices `assigns` (in order) and returns (their values,
+        the position of the best -- strictly better replaces, so the first
+        wins a tie --, its slot).  The best slice's intermediates stay on the
+        device for grad_best_into.  Each value is judged while the next slice
+        runs (an asynchronous copy to pinned memory and an event), so the
+        device never waits for the host."""
+        import torch
+        if not assigns:
+            return [], -1, None
+        slots = self._value_slots(assigns[0])
+        dev = torch.device(f"cuda:{self.be.device}")
+        stream = torch.cuda.ExternalStream(self.be.stream(), device=dev)
+        tdt = torch.float64 if self.dtype == np.float64 else torch.float32
+        n = len(assigns)
+        es = np.dtype(self.dtype).itemsize
+        with torch.cuda.stream(stream):
+            res = torch.empty(n, dtype=tdt, device=dev)
+            host = torch.empty(n, dtype=tdt, pin_memory=True)
+        free = list(range(len(slots)))
+        best = (None, -1, None)  # (key, position, slot)
+        pending = None  # (position, slot, event)
+        vals = [None] * n
+
+        def judge(p):
+            nonlocal best
+            q, s_, ev = p
+            ev.synchronize()
+            v = float(host[q])
+            vals[q] = v
+            k = order_key(v, minimize)
+            if best[0] is None or k > best[0]:
+                if best[2] is not None:
+                    free.append(best[2])
+                best = (k, q, s_)
+            else:
+                free.append(s_)
+
+        for q, a in enumerate(assigns):
+            s_ = free.pop()
+            plan = slots[s_]
+            self._prepare(plan, a)
+            plan["graph"].launch()
+            self.be.copy_device(res.data_ptr() + q * es, plan["out"].ptr, es)
+            with torch.cuda.stream(stream):
+                host[q:q + 1].copy_(res[q:q + 1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(stream)
+            if pending is not None:
+                judge(pending)
+            pending = (q, s_, ev)
+        judge(pending)
+        return vals, best[1], best[2]
+
+    def grad_best_into(self, assign, slot, layout, dst_ptr, dy=1.0):
+        """Gradient of the slice best_of kept in `slot` (its assignment
+        `assign`), found by the values-only backward through its tape and the
+        hoisted subtrees' tapes, placed with its value into dst_ptr as
+        grad_into does.  No forward runs again."""
+        key = frozenset(assign.keys())
+        plan = self._vslots[key][slot]
+        om = sys.modules[type(self.be).__module__]
+        L = om.lib()
+        dt = om.DTYPES[np.dtype(self.dtype)]
+        if "gbufs" not in plan:
+            plan["gbufs"] = self._grad_buffers(plan, key)
+            plan["dy"] = self.be.alloc(1, self.dtype)
+            plan["dy_val"] = None
+        grads, sub_grads, gbuf, _ = plan["gbufs"]
+        if plan["dy_val"] != dy:
+            self.be.upload_into(plan["dy"], np.asarray([dy], self.dtype))
+            plan["dy_val"] = dy
+        leaves = self._reduce(key)[0]
+        links = [(j, lf[3], sg) for j, (lf, sg) in enumerate(zip(leaves, sub_grads))
+                 if lf[0] == "hoisted"]
+        self.E.Einsum.backward_tape_linked(plan["tape"], plan["dy"], grads, links)
+        idx = self.place_index(layout, assign)
+        om._check(L.om_b200_scatter_index(self.be.h, dt, gbuf.ptr, len(idx), idx.ptr, dst_ptr, 0))
+        if "zero_idx" not in self.__dict__:
+            self.zero_idx = self.be.from_slice(np.zeros(1, np.int64))
+        om._check(L.om_b200_scatter_index(self.be.h, dt, plan["out"].ptr, 1, self.zero_idx.ptr,
+                                          dst_ptr, 0))
+
     def _gbuf_order(self, key):
         """Input tensor of each region of the gradient buffer, in buffer order
         (the reduced tree's leaves, then each hoisted subtree's leaves)."""
@@ -600,6 +710,13 @@ class DeviceExecutor:
                     self.E.Einsum.tape_free(sp["tape"])
                 except Exception:
                     pass
+        for slots in getattr(self, "_vslots", {}).values():
+            for plan in slots:
+                if plan.get("tape") is not None:
+                    try:
+                        plan["ein"].tape_free(plan["tape"])
+                    except Exception:
+                        pass
         for gp in getattr(self, "_grad_plans", {}).values():
             if gp.get("tape") is not None:
                 try:
@@ -737,12 +854,18 @@ class CombineError(RuntimeError):
 
 
 def _collective(dist, op, timeout_s, what):
-    """Runs `op(async_op=True)` and waits at most timeout_s for it."""
-    import datetime
+    """Runs `op(async_op=True)` and waits at most timeout_s for it, polling
+    its completion every ~20 us (a timed Work.wait may sleep in coarse steps,
+    which would add milliseconds to every combine)."""
+    import time
     try:
         work = op(async_op=True)
-        if not work.wait(timeout=datetime.timedelta(seconds=timeout_s)):
-            raise CombineError(f"{what}: not completed within {timeout_s} s")
+        deadline = time.monotonic() + timeout_s
+        while not work.is_completed():
+            if time.monotonic() > deadline:
+                raise CombineError(f"{what}: not completed within {timeout_s} s")
+            time.sleep(2e-5)
+        work.wait()
     except CombineError:
         raise
     except Exception as e:  # gloo / NCCL report a lost peer or a timeout
@@ -786,7 +909,11 @@ def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device
     if alg in TROPICAL:
         minimize = TROPICAL[alg]
         best = None
-        if hasattr(executor, "values"):
+        best_slot = None
+        if on_device and executor.use_graph and mine:
+            # values at value cost, the best slice's intermediates kept
+            vals, bpos, best_slot = executor.best_of([assigns[s] for s in mine], minimize)
+        elif hasattr(executor, "values"):
             vals = executor.values([assigns[s] for s in mine])
         else:
             vals = [executor.value(assigns[s]) for s in mine]
@@ -809,7 +936,10 @@ def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device
             with ctx:  # every device step on the backend's stream
                 buf = torch.zeros(1 + layout.total, dtype=tdt, device=device)
                 if owner == rank:
-                    executor.grad_into(assigns[win], layout, buf.data_ptr(), accumulate=False)
+                    if best_slot is not None:  # the winner is this rank's best slice
+                        executor.grad_best_into(assigns[win], best_slot, layout, buf.data_ptr())
+                    else:
+                        executor.grad_into(assigns[win], layout, buf.data_ptr(), accumulate=False)
                 if multi:
                     _collective(dist, lambda **kw: dist.broadcast(buf, src=owner, **kw),
                                 timeout_s, "gradient broadcast")
