@@ -41,7 +41,10 @@ typedef enum {
   OM_MAXMUL = 3    /* (max, x) zero 0            */
 } om_algebra;
 
-typedef enum { OM_F32 = 0, OM_F64 = 1, OM_U32 = 2 } om_dtype;
+/* OM_C32 / OM_C64: complex numbers as interleaved (re, im) pairs of
+ * f32 / f64 (the layout of num_complex::Complex and of the reference's
+ * CudaComplex, src/backend/cuda/mod.rs:56-208); Standard algebra only. */
+typedef enum { OM_F32 = 0, OM_F64 = 1, OM_U32 = 2, OM_C32 = 3, OM_C64 = 4 } om_dtype;
 
 enum {
   OM_OK = 0,

@@ -27,8 +27,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libomeinsum_b200.so")
 
 ALGEBRAS = {"standard": 0, "maxplus": 1, "minplus": 2, "maxmul": 3}
-DTYPES = {np.dtype(np.float32): 0, np.dtype(np.float64): 1, np.dtype(np.uint32): 2}
-NP_OF = {0: np.float32, 1: np.float64, 2: np.uint32}
+DTYPES = {np.dtype(np.float32): 0, np.dtype(np.float64): 1, np.dtype(np.uint32): 2,
+          np.dtype(np.complex64): 3, np.dtype(np.complex128): 4}
+NP_OF = {0: np.float32, 1: np.float64, 2: np.uint32, 3: np.complex64, 4: np.complex128}
 
 # every symbol the header declares (checked by the CPU test suite)
 EXPORTS = [

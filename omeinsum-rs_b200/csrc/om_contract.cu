@@ -555,6 +555,82 @@ int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Op
 
 }  // namespace om
 
+namespace om {
+namespace {
+
+// C = re(T[0,0]) - T[1,1] + i (T[0,1] + T[1,0]) for every output element;
+// T is [2 (A part)][2 (B part)][n] column-major
+template <typename R>
+__global__ void complex_combine_kernel(const R* __restrict__ t, R* __restrict__ c, int64_t n) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const R* q = t + 4 * e;
+    c[2 * e] = q[0] - q[3];
+    c[2 * e + 1] = q[2] + q[1];
+  }
+}
+
+// A complex operand seen as a real one: a leading part mode (re, im) of
+// extent 2 and stride 1, every other stride doubled.
+Operand real_view(const Operand& X, int32_t part) {
+  Operand R;
+  R.modes.push_back(part);
+  R.shape.push_back(2);
+  R.strides.push_back(1);
+  for (size_t i = 0; i < X.modes.size(); ++i) {
+    R.modes.push_back(X.modes[i]);
+    R.shape.push_back(X.shape[i]);
+    R.strides.push_back(2 * X.strides[i]);
+  }
+  return R;
+}
+
+}  // namespace
+
+// Standard complex contraction through the real planner: with A and B as
+// real operands carrying their own part mode (pa, pb), one real contraction
+// gives T[pa, pb, c...] = sum_k A_pa B_pb (all four products of parts, on
+// whatever real path the shape takes -- the tensor cores for f32), and a
+// combine pass forms re = T00 - T11, im = T01 + T10.
+int contract_complex(om_backend* be, om_algebra alg, om_dtype dt, const void* a, const Operand& A,
+                     const void* b, const Operand& B, const Operand& C, void* c_out,
+                     uint32_t* argmax) {
+  if (alg != OM_STANDARD)
+    return set_error(OM_ERR_UNSUPPORTED, "contract: complex dtypes take the Standard algebra only");
+  int32_t top = 0;
+  for (const Operand* op : {&A, &B, &C})
+    for (auto m : op->modes) top = std::max(top, m);
+  if (top > INT32_MAX - 2) return set_error(OM_ERR_INVALID, "contract: mode labels too large");
+  const int32_t pa = top + 1, pb = top + 2;
+  const om_dtype rt = real_part(dt);
+  const size_t rs = dtype_size(rt);
+  Operand RA = real_view(A, pa), RB = real_view(B, pb), RT;
+  RT.modes = {pa, pb};
+  RT.shape = {2, 2};
+  int64_t n = 1;
+  for (size_t i = 0; i < C.modes.size(); ++i) {
+    RT.modes.push_back(C.modes[i]);
+    RT.shape.push_back(C.shape[i]);
+    n *= C.shape[i];
+  }
+  if (argmax && n > 0)
+    OM_CUDA(cudaMemsetAsync(argmax, 0, 4 * (size_t)n, be->stream), "argmax zero");
+  if (n == 0) return OM_OK;
+  Scratch t;
+  OM_TRY(t.alloc(be, rs * 4 * (size_t)n));
+  OM_TRY(contract_impl(be, OM_STANDARD, rt, a, RA, b, RB, RT, t.ptr, nullptr));
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)be->num_sms * 8));
+  ProfScope prof(be, "complex_combine");
+  if (rt == OM_F32)
+    complex_combine_kernel<float><<<blocks, 256, 0, be->stream>>>((const float*)t.ptr, (float*)c_out, n);
+  else
+    complex_combine_kernel<double><<<blocks, 256, 0, be->stream>>>((const double*)t.ptr, (double*)c_out, n);
+  note_launch();
+  return check_cuda(cudaGetLastError(), "complex combine launch");
+}
+
+}  // namespace om
+
 extern "C" int om_b200_contract(om_backend* be, om_algebra alg, om_dtype dtype, const void* a,
                                 int nda, const int64_t* shape_a, const int64_t* strides_a,
                                 const int32_t* modes_a, const void* b, int ndb,
@@ -568,8 +644,8 @@ extern "C" int om_b200_contract(om_backend* be, om_algebra alg, om_dtype dtype, 
   if ((nda && (!shape_a || !strides_a || !modes_a)) || (ndb && (!shape_b || !strides_b || !modes_b)) ||
       (ndc && (!shape_c || !modes_c)))
     return set_error(OM_ERR_INVALID, "om_b200_contract: null shape/stride/mode array");
-  if (dtype != OM_F32 && dtype != OM_F64)
-    return set_error(OM_ERR_UNSUPPORTED, "om_b200_contract: dtype must be OM_F32 or OM_F64");
+  if (dtype != OM_F32 && dtype != OM_F64 && !is_complex(dtype))
+    return set_error(OM_ERR_UNSUPPORTED, "om_b200_contract: dtype must be OM_F32, OM_F64, OM_C32 or OM_C64");
   OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
   Operand A, B, C;
   A.modes.assign(modes_a, modes_a + nda);
@@ -580,5 +656,6 @@ extern "C" int om_b200_contract(om_backend* be, om_algebra alg, om_dtype dtype, 
   B.strides.assign(strides_b, strides_b + ndb);
   C.modes.assign(modes_c, modes_c + ndc);
   C.shape.assign(shape_c, shape_c + ndc);
+  if (is_complex(dtype)) return contract_complex(be, alg, dtype, a, A, b, B, C, c_out, argmax_out);
   return contract_impl(be, alg, dtype, a, A, b, B, C, c_out, argmax_out);
 }

@@ -831,8 +831,9 @@ static int einsum_impl(om_backend* be, om_algebra alg, om_dtype dtype, int ntens
   if (!be || !tensors || !ndims || !out || ntensors < 1 || niy < 0 || nnodes < 0 ||
       (nnodes > 0 && (!children || !node_iy_off)))
     return set_error(OM_ERR_INVALID, "om_b200_einsum: bad argument");
-  if (dtype != OM_F32 && dtype != OM_F64)
-    return set_error(OM_ERR_UNSUPPORTED, "om_b200_einsum: dtype must be f32 or f64");
+  if (dtype != OM_F32 && dtype != OM_F64 && !(is_complex(dtype) && alg == OM_STANDARD))
+    return set_error(OM_ERR_UNSUPPORTED,
+                     "om_b200_einsum: dtype must be f32 or f64 (complex: Standard algebra only)");
   if (nnodes == 0 && ntensors != 1)
     return set_error(OM_ERR_INVALID, "om_b200_einsum: a tree without nodes needs exactly one tensor");
   if (nnodes > 0 && nnodes != ntensors - 1)

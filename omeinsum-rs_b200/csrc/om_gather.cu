@@ -538,6 +538,16 @@ extern "C" int om_b200_copy_strided(om_backend* be, om_dtype dtype, const void* 
   if (!be || !src || !dst || (ndim > 0 && (!shape || !strides)))
     return set_error(OM_ERR_INVALID, "om_b200_copy_strided: null argument");
   OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  if (is_complex(dtype)) {  // the two parts as a leading unit-stride axis of extent 2
+    if (ndim < 0 || ndim + 1 > OM_MAX_DIMS) return set_error(OM_ERR_INVALID, "gather: bad rank");
+    std::vector<int64_t> sh{2}, st{1};
+    for (int k = 0; k < ndim; ++k) {
+      sh.push_back(shape[k]);
+      st.push_back(2 * strides[k]);
+    }
+    return launch_gather(be, dtype_size(real_part(dtype)), src, ndim + 1, sh.data(), st.data(),
+                         2 * offset, dst);
+  }
   return launch_gather(be, dtype_size(dtype), src, ndim, shape, strides, offset, dst);
 }
 

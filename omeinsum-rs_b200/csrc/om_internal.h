@@ -67,7 +67,12 @@ struct ProfScope {
 
 #define OM_CUDA(expr, what) OM_TRY(::om::check_cuda((expr), (what)))
 
-inline size_t dtype_size(om_dtype dt) { return dt == OM_F64 ? 8 : 4; }
+inline size_t dtype_size(om_dtype dt) {
+  return dt == OM_C64 ? 16 : (dt == OM_F64 || dt == OM_C32) ? 8 : 4;
+}
+inline bool is_complex(om_dtype dt) { return dt == OM_C32 || dt == OM_C64; }
+// the real type of a complex dtype's parts
+inline om_dtype real_part(om_dtype dt) { return dt == OM_C64 ? OM_F64 : OM_F32; }
 
 // ---- device memory of the library's own buffers --------------------------
 // Outside a recording: the device's stream-ordered pool (cudaMallocAsync /

@@ -13,6 +13,7 @@
 // One thread per output element; the inner loop runs in the reference's order.
 #include <algorithm>
 #include <map>
+#include <vector>
 
 #include "om_internal.h"
 #include "om_semiring.cuh"
@@ -100,6 +101,34 @@ int launch_unary(om_backend* be, om_algebra alg, om_dtype dt, const void* x, int
                  const int32_t* iy, const int64_t* sizes_y, void* y, uint32_t* argmax) {
   if (nx < 0 || ny < 0 || nx > OM_MAX_DIMS || ny > OM_MAX_DIMS)
     return set_error(OM_ERR_INVALID, "unary: rank out of range");
+  if (is_complex(dt)) {
+    // Standard sums act on the real and imaginary parts alike: a real unary
+    // einsum with a part label (extent 2, stride 1) kept in front
+    if (alg != OM_STANDARD)
+      return set_error(OM_ERR_UNSUPPORTED, "unary: complex dtypes take the Standard algebra only");
+    if (nx + 1 > OM_MAX_DIMS || ny + 1 > OM_MAX_DIMS)
+      return set_error(OM_ERR_INVALID, "unary: rank out of range");
+    int32_t top = 0;
+    for (int k = 0; k < nx; ++k) top = std::max(top, ix[k]);
+    for (int k = 0; k < ny; ++k) top = std::max(top, iy[k]);
+    std::vector<int32_t> rix{top + 1}, riy{top + 1};
+    std::vector<int64_t> rsh{2}, rst{1}, rsy{2};
+    for (int k = 0; k < nx; ++k) {
+      rix.push_back(ix[k]);
+      rsh.push_back(shape_x[k]);
+      rst.push_back(2 * strides_x[k]);
+    }
+    for (int k = 0; k < ny; ++k) {
+      riy.push_back(iy[k]);
+      rsy.push_back(sizes_y[k]);
+    }
+    int64_t nout = 1;
+    for (int k = 0; k < ny; ++k) nout *= sizes_y[k];
+    if (argmax && nout > 0)
+      OM_CUDA(cudaMemsetAsync(argmax, 0, 4 * (size_t)nout, be->stream), "argmax zero");
+    return launch_unary(be, alg, real_part(dt), x, nx + 1, rix.data(), rsh.data(), rst.data(),
+                        ny + 1, riy.data(), rsy.data(), y, nullptr);
+  }
   UnaryDesc d{};
   std::map<int32_t, int> slot;
   std::map<int32_t, int64_t> size;
