@@ -159,6 +159,24 @@ int om_b200_scatter_index(om_backend* be, om_dtype dtype, const void* src, int64
 int om_b200_gather_views(om_backend* be, om_dtype dtype, int nviews, const int64_t* desc,
                          const int64_t* offsets, const int32_t* sel, int64_t max_numel);
 
+/* Contraction-order optimisation by tree simulated annealing (host code;
+ * replaces the reference's call into omeco's optimize_treesa,
+ * src/einsum/engine.rs:84-91).  Network as in om_b200_einsum (ntensors,
+ * ndims, ixs, iy, size dictionary).  init_children (2 * (ntensors - 1),
+ * post order, may be NULL) seeds the first of ntrials runs; the others start
+ * from random trees.  Cost: log2 sum of 2^tc over nodes + sc_weight * sum
+ * of max(0, log2 size - sc_target) over intermediates + rw_weight * log2 of
+ * the read-write volume; Metropolis moves (rotations at a node), beta from
+ * beta_start to beta_end by beta_step, niters sweeps per beta.  Writes the
+ * best tree to children_out (post order) and its log2 time / space
+ * complexity to tc_out / sc_out (may be NULL). */
+int om_b200_optimize_tree(int ntensors, const int32_t* ndims, const int32_t* ixs, int niy,
+                          const int32_t* iy, int nsizes, const int32_t* size_labels,
+                          const int64_t* size_values, const int32_t* init_children,
+                          double sc_target, double sc_weight, double rw_weight, int ntrials,
+                          int niters, double beta_start, double beta_end, double beta_step,
+                          uint64_t seed, int32_t* children_out, double* tc_out, double* sc_out);
+
 /* Kernel launches issued by this thread since the last call (counter reset
  * on read); used by benchmarks to report how many device kernels ran. */
 int64_t om_b200_launch_count(void);

@@ -40,7 +40,7 @@ EXPORTS = [
     "om_b200_tropical_matmul_argmax_noalloc", "om_b200_einsum", "om_b200_einsum_backward",
     "om_b200_tape_free", "om_b200_graph_begin", "om_b200_graph_end", "om_b200_graph_launch",
     "om_b200_graph_free", "om_b200_tape_release", "om_b200_einsum_backward_linked",
-    "om_b200_set_f32_mode", "om_b200_scatter_index", "om_b200_gather_views", "om_b200_einsum_tape_values",
+    "om_b200_set_f32_mode", "om_b200_scatter_index", "om_b200_gather_views", "om_b200_einsum_tape_values", "om_b200_optimize_tree",
 ]
 
 

@@ -434,24 +434,58 @@ int launch_gemm_exact(om_backend* be, const GemmArgs& g) {
 }
 
 // A node with few outputs and a long contracted range (the root of a network
-// is often a dot product of two large intermediates): one CTA per output,
-// each thread reduces a contiguous run of k, and thread 0 combines the runs
-// in k order.  The tropical combine reproduces the sequential rule of
-// generic_gemm_with_argmax exactly: a run is summarised by its first best
-// element taken from an empty start (what the sequential rule holds after the
-// run from any incoming value it replaces), or, when the run holds a NaN
-// product, by the state after its last NaN (which no earlier value survives).
-constexpr int kSplitThreads = 256;
+// is often a dot product of two large intermediates; annealed trees also
+// contract two large intermediates into a few thousand outputs): one CTA per
+// output, the threads interleaved over k so that a warp reads consecutive
+// k.  The offsets of the low contracted modes (up to kSplitTable k values)
+// sit in a shared-memory table; the high modes are decoded once per table
+// pass.  Tropical: each thread keeps its first best element (strict
+// improvement, k visited in increasing order), and the merge takes the
+// better value, then the smaller k -- the first k reaching the maximum, as
+// the sequential rule of generic_gemm_with_argmax gives.  A NaN product
+// breaks that equivalence (the sequential rule lets a NaN replace the
+// accumulator and the next product replace the NaN), so an output that meets
+// one is recomputed sequentially by thread 0.  Standard: a tree sum.
+constexpr int kSplitThreads = 256, kSplitTable = 2048;
 
 template <typename T, int ALG, bool ARGMAX>
-__global__ void __launch_bounds__(kSplitThreads) gemm_node_splitk(NodeArgs g) {
+__global__ void __launch_bounds__(kSplitThreads) gemm_node_splitk(NodeArgs g, int nklo,
+                                                                  int64_t klo) {
   using S = Semi<ALG, T>;
-  __shared__ T sv[kSplitThreads];
-  __shared__ uint32_t si[kSplitThreads];
-  __shared__ uint8_t sf[kSplitThreads];  // bit 0: run not empty, bit 1: run reset by a NaN
-  const int tid = threadIdx.x;
+  __shared__ int64_t ta[kSplitTable], tb[kSplitTable];
+  __shared__ T sv[kSplitThreads / 32];
+  __shared__ int64_t sk[kSplitThreads / 32];
+  __shared__ int snan;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int k = tid; k < (int)klo; k += kSplitThreads) {
+    uint32_t r = (uint32_t)k;
+    int64_t xa = 0, xb = 0;
+    for (int j = 0; j < nklo; ++j) {
+      const uint32_t q = fast_div(r, g.kmodes[j].div);
+      const uint32_t d = r - q * g.kmodes[j].div.d;
+      xa += (int64_t)d * g.kmodes[j].sa;
+      xb += (int64_t)d * g.kmodes[j].sb;
+      r = q;
+    }
+    ta[k] = xa;
+    tb[k] = xb;
+  }
+  __syncthreads();
   const T* __restrict__ A = (const T*)g.A;
   const T* __restrict__ B = (const T*)g.B;
+  const int64_t khi_n = g.K / klo;
+  auto prod_at = [&](int64_t oa, int64_t ob, int64_t k) {
+    uint32_t r = (uint32_t)k;
+    int64_t xa = oa, xb = ob;
+    for (int j = 0; j < g.nk; ++j) {
+      const uint32_t q = fast_div(r, g.kmodes[j].div);
+      const uint32_t d = r - q * g.kmodes[j].div.d;
+      xa += (int64_t)d * g.kmodes[j].sa;
+      xb += (int64_t)d * g.kmodes[j].sb;
+      r = q;
+    }
+    return ALG == OM_STANDARD ? A[xa] * B[xb] : S::mul(A[xa], B[xb]);
+  };
   for (int64_t o = blockIdx.x; o < g.total; o += gridDim.x) {
     int64_t oa = 0, ob = 0;
     {
@@ -464,53 +498,79 @@ __global__ void __launch_bounds__(kSplitThreads) gemm_node_splitk(NodeArgs g) {
         r = q;
       }
     }
-    const int64_t per = (g.K + kSplitThreads - 1) / kSplitThreads;
-    const int64_t k0 = tid * per, k1 = k0 + per < g.K ? k0 + per : g.K;
     T acc = ALG == OM_STANDARD ? T(0) : S::zero();
-    uint32_t idx = 0;
-    uint8_t flag = 0;
-    for (int64_t k = k0; k < k1; ++k) {
-      uint32_t r = (uint32_t)k;
-      int64_t xa = oa, xb = ob;
-      for (int j = 0; j < g.nk; ++j) {
+    int64_t bk = INT64_MAX;
+    bool nan = false;
+    for (int64_t h = 0; h < khi_n; ++h) {
+      uint32_t r = (uint32_t)h;
+      int64_t ha = oa, hb = ob;
+      for (int j = nklo; j < g.nk; ++j) {
         const uint32_t q = fast_div(r, g.kmodes[j].div);
         const uint32_t d = r - q * g.kmodes[j].div.d;
-        xa += (int64_t)d * g.kmodes[j].sa;
-        xb += (int64_t)d * g.kmodes[j].sb;
+        ha += (int64_t)d * g.kmodes[j].sa;
+        hb += (int64_t)d * g.kmodes[j].sb;
         r = q;
       }
-      if (ALG == OM_STANDARD) {
-        acc = fma(A[xa], B[xb], acc);
-      } else {
-        const T p = S::mul(A[xa], B[xb]);
-        if (!(flag & 1) || !S::keep(acc, p)) {
-          acc = p;
-          idx = (uint32_t)k;
+      for (int k = tid; k < (int)klo; k += kSplitThreads) {
+        const T av = A[ha + ta[k]], bv = B[hb + tb[k]];
+        if (ALG == OM_STANDARD) {
+          acc = fma(av, bv, acc);
+        } else {
+          const T p = S::mul(av, bv);
+          nan |= p != p;
+          if (S::better(p, acc)) {  // visited in increasing k: the first best stays
+            acc = p;
+            bk = h * klo + k;
+          }
         }
-        flag |= 1;
-        if (p != p) flag |= 2;
       }
     }
-    sv[tid] = acc;
-    si[tid] = idx;
-    sf[tid] = flag;
-    __syncthreads();
-    if (tid == 0) {
-      T v = ALG == OM_STANDARD ? T(0) : S::zero();
-      uint32_t w = 0;
-      for (int t = 0; t < kSplitThreads; ++t) {
-        if (ALG == OM_STANDARD) {
-          v += sv[t];
-        } else if (sf[t] & 2) {
-          v = sv[t];
-          w = si[t];
-        } else if ((sf[t] & 1) && !S::keep(v, sv[t])) {
-          v = sv[t];
-          w = si[t];
+    // merge: warps, then the block
+    for (int sh = 16; sh; sh >>= 1) {
+      const T ov = __shfl_xor_sync(0xffffffffu, acc, sh);
+      if (ALG == OM_STANDARD) {
+        acc += ov;
+      } else {
+        const int64_t okk = __shfl_xor_sync(0xffffffffu, bk, sh);
+        if (S::better(ov, acc) || (ov == acc && okk < bk)) {
+          acc = ov;
+          bk = okk;
         }
       }
+    }
+    if (tid == 0) snan = 0;
+    __syncthreads();
+    if (nan) snan = 1;
+    if (lane == 0) {
+      sv[warp] = acc;
+      sk[warp] = bk;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      T v = sv[0];
+      int64_t w = sk[0];
+      for (int q = 1; q < kSplitThreads / 32; ++q) {
+        if (ALG == OM_STANDARD) {
+          v += sv[q];
+        } else if (S::better(sv[q], v) || (sv[q] == v && sk[q] < w)) {
+          v = sv[q];
+          w = sk[q];
+        }
+      }
+      if (ALG != OM_STANDARD && snan) {  // the sequential rule, as in the forward
+        v = S::zero();
+        w = 0;
+        for (int64_t k = 0; k < g.K; ++k) {
+          const T p = prod_at(oa, ob, k);
+          if (!S::keep(v, p)) {
+            v = p;
+            w = k;
+          }
+        }
+      }
+      if (ALG != OM_STANDARD && w == INT64_MAX) w = 0;  // nothing beat zero()
       ((T*)g.C)[o] = v;
-      if (ARGMAX) g.argmax[o] = w;
+      if (ARGMAX) g.argmax[o] = ALG == OM_STANDARD ? 0u : (uint32_t)w;
     }
     __syncthreads();
   }
@@ -520,19 +580,24 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
   if (g0.total <= 0) return OM_OK;
   if (g0.K >= (int64_t(1) << 32) || g0.nout > kMaxNodeModes || g0.nk > kMaxNodeModes)
     return set_error(OM_ERR_INVALID, "gemm_node: plan out of range");
-  if (g0.K >= 2048 && g0.total <= 4 * (int64_t)be->num_sms) {
-    // few outputs, long k: split the k range of each output over a CTA
-    const int grid = (int)g0.total;
+  if (g0.K >= 2048 && g0.total <= 64 * (int64_t)be->num_sms) {
+    // few outputs, long k: the k range of each output over a CTA; the low
+    // contracted modes whose extents multiply to at most kSplitTable are
+    // tabulated
+    int nklo = 0;
+    int64_t klo = 1;
+    while (nklo < g0.nk && klo * g0.kmodes[nklo].div.d <= kSplitTable) klo *= g0.kmodes[nklo++].div.d;
+    const int grid = (int)std::min<int64_t>(g0.total, (int64_t)be->num_sms * 64);
     ProfScope prof(be, "gemm_node_splitk");
     if (g0.dtype == OM_F32) {
       OM_DISPATCH_ALG(g0.alg, ALG, {
-        if (g0.argmax) gemm_node_splitk<float, ALG, true><<<grid, kSplitThreads, 0, be->stream>>>(g0);
-        else gemm_node_splitk<float, ALG, false><<<grid, kSplitThreads, 0, be->stream>>>(g0);
+        if (g0.argmax) gemm_node_splitk<float, ALG, true><<<grid, kSplitThreads, 0, be->stream>>>(g0, nklo, klo);
+        else gemm_node_splitk<float, ALG, false><<<grid, kSplitThreads, 0, be->stream>>>(g0, nklo, klo);
       });
     } else {
       OM_DISPATCH_ALG(g0.alg, ALG, {
-        if (g0.argmax) gemm_node_splitk<double, ALG, true><<<grid, kSplitThreads, 0, be->stream>>>(g0);
-        else gemm_node_splitk<double, ALG, false><<<grid, kSplitThreads, 0, be->stream>>>(g0);
+        if (g0.argmax) gemm_node_splitk<double, ALG, true><<<grid, kSplitThreads, 0, be->stream>>>(g0, nklo, klo);
+        else gemm_node_splitk<double, ALG, false><<<grid, kSplitThreads, 0, be->stream>>>(g0, nklo, klo);
       });
     }
     note_launch();

@@ -31,6 +31,10 @@ def _bind():
         L.om_b200_tape_free.argtypes = [P]
         L.om_b200_tape_release.argtypes = [P]
         L.om_b200_einsum_backward_linked.argtypes = [P, P, P, I, P, P, P]
+        D = ctypes.c_double
+        L.om_b200_optimize_tree.argtypes = [I, P, P, I, P, I, P, P, P, D, D, D, I, I, D, D, D,
+                                            ctypes.c_uint64, P, ctypes.POINTER(D),
+                                            ctypes.POINTER(D)]
         L._einsum_bound = True
     return L
 
@@ -111,6 +115,44 @@ def greedy_tree(ixs, iy, sizes):
             count[l] += 1
         items = [it for k, it in enumerate(items) if k not in (pa, pb)] + [((ta, tb), out)]
     return items[0][0]
+
+
+def decode_tree(children, n):
+    """Nested-tuple tree of a post-order children array (inverse of the
+    children part of encode_tree)."""
+    nodes = []
+    for i in range(len(children) // 2):
+        a, b = children[2 * i], children[2 * i + 1]
+        nodes.append((a if a < n else nodes[a - n], b if b < n else nodes[b - n]))
+    return nodes[-1] if nodes else 0
+
+
+def treesa_tree(ixs, iy, sizes, init=None, sc_target=20.0, sc_weight=1.0, rw_weight=0.0,
+                ntrials=4, niters=10, betas=(0.01, 15.0, 0.05), seed=0):
+    """Tree simulated annealing (om_b200_optimize_tree, the replacement of
+    omeco's optimize_treesa called at src/einsum/engine.rs:84-91): returns
+    (tree, log2 tc, log2 sc).  init: a starting tree for the first trial
+    (the others start from random trees)."""
+    L = _bind()
+    n = len(ixs)
+    if n < 2:
+        return 0, 0.0, 0.0
+    nd = _i32([len(ix) for ix in ixs])
+    flat = _i32([l for ix in ixs for l in ix])
+    iya = _i32(list(iy))
+    sl = _i32(list(sizes.keys()))
+    sv = _i64(list(sizes.values()))
+    ch0 = None
+    if init is not None:
+        ch0 = _i32(encode_tree(init, ixs, iy)[0])
+    out = _i32([0] * (2 * (n - 1)))
+    tc, sc = ctypes.c_double(), ctypes.c_double()
+    _check(L.om_b200_optimize_tree(n, _p(nd), _p(flat), len(iya), _p(iya), len(sl), _p(sl),
+                                   _p(sv), None if ch0 is None else _p(ch0), sc_target,
+                                   sc_weight, rw_weight, ntrials, niters, betas[0], betas[1],
+                                   betas[2], seed, _p(out), ctypes.byref(tc),
+                                   ctypes.byref(sc)))
+    return decode_tree([int(x) for x in out], n), tc.value, sc.value
 
 
 def tree_cost(tree, ixs, iy, sizes):

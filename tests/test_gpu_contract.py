@@ -388,7 +388,7 @@ def test_graph_replay_of_contractions(be):
 
 @pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul", "standard"])
 @pytest.mark.parametrize("special", ["ties", "nan_inf", "normal"])
-@pytest.mark.parametrize("nout", [1, 3])
+@pytest.mark.parametrize("nout", [1, 3, 700])
 def test_long_k_few_outputs_split_k(be, alg, special, nout):
     """Nodes with a handful of outputs and a long contracted range (a
     network's root dot product) split k over a CTA; the tropical combine must
