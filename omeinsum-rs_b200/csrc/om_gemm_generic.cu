@@ -225,8 +225,19 @@ __device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], 
   for (int i = 0; i < V; ++i) out[i] = p[off[i]];
 }
 
+// Blocks per SM for a gemm_node variant: its inner step holds 2 * k * V
+// operand values in registers (k = KT, or the chunk of four of the generic
+// path) besides its state (about 24 registers; 48 for single outputs, which
+// keep 64-bit offsets), which sets the register cap.
+template <typename T, int KT, int V>
+constexpr int node_min_blocks() {
+  constexpr int regs = 2 * (KT == 0 ? 4 : KT) * V * (int)(sizeof(T) / 4) + (V == 1 ? 48 : 24);
+  constexpr int b = 65536 / (256 * regs);
+  return b > 8 ? 8 : (b < 2 ? 2 : b);
+}
+
 template <typename T, int ALG, bool ARGMAX, int KT, int V>
-__global__ void __launch_bounds__(256, 8) gemm_node(NodeArgs g) {
+__global__ void __launch_bounds__(256, (node_min_blocks<T, KT, V>())) gemm_node(NodeArgs g) {
   using S = Semi<ALG, T>;
   // four-output groups run on 32-bit offsets (the launcher checks that
   // every offset of both operands fits); single outputs keep 64-bit ones
@@ -317,13 +328,39 @@ __global__ void __launch_bounds__(256, 8) gemm_node(NodeArgs g) {
               }
             }
           }
+      } else if (ktab) {
+        // tabulated k in chunks of four: the chunk's loads go out together
+        // and a group of V outputs loads as one vector where it can
+        for (int k0 = 0; k0 < (int)g.K; k0 += 4) {
+          const int kn = (int)g.K - k0 < 4 ? (int)g.K - k0 : 4;
+          T av[4][V], bv[4][V];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (k < kn) {
+              load_group<V>(a + ka[k0 + k], g.ia, g.wa, av[k]);
+              load_group<V>(b + kb[k0 + k], g.ib, g.wb, bv[k]);
+            }
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (k < kn) {
+#pragma unroll
+              for (int i = 0; i < V; ++i) {
+                if (ALG == OM_STANDARD) {
+                  acc[i] = fma(av[k][i], bv[k][i], acc[i]);
+                } else {
+                  const T p = S::mul(av[k][i], bv[k][i]);
+                  if (!S::keep(acc[i], p)) {
+                    acc[i] = p;
+                    idx[i] = (uint32_t)(k0 + k);
+                  }
+                }
+              }
+            }
+        }
       } else {
         for (int64_t k = 0; k < g.K; ++k) {
           int64_t xa, xb;
-          if (ktab) {
-            xa = ka[k];
-            xb = kb[k];
-          } else {
+          {
             xa = xb = 0;
             uint32_t rk = (uint32_t)k;
             for (int j = 0; j < g.nk; ++j) {
@@ -608,6 +645,34 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
   // to 4 * kNodeQuads outputs
   NodeArgs g = g0;
   const size_t es = dtype_size(g.dtype);
+  // A tile row spans the leading output modes while their product stays
+  // within kNodeQuads * 4; a large mode that would end the row early (a
+  // leading 2 x 2 and then an extent of 2^21 leaves rows of four outputs,
+  // each decoding every high mode) is split into two modes, f x e / f, with
+  // f the largest divisor of its extent that fills the row.  Linear output
+  // order is unchanged (the first factor runs fastest).
+  {
+    int64_t P = 1;
+    const int64_t L = (int64_t)kNodeQuads * 4;
+    for (int j = 0; j < g.nout; ++j) {
+      const int64_t e = g.out[j].div.d;
+      if (P * e <= L) {
+        P *= e;
+        continue;
+      }
+      if (P * 64 > L || g.nout >= kMaxNodeModes) break;  // the row is long enough
+      int64_t f = L / P;
+      while (f > 1 && e % f) --f;
+      if (f > 1) {
+        for (int q = g.nout; q > j + 1; --q) g.out[q] = g.out[q - 1];
+        const NodeMode m = g.out[j];
+        g.out[j] = NodeMode{make_fastdiv((uint32_t)f), m.sa, m.sb};
+        g.out[j + 1] = NodeMode{make_fastdiv((uint32_t)(e / f)), m.sa * f, m.sb * f};
+        ++g.nout;
+      }
+      break;
+    }
+  }
   // a group of 4 consecutive outputs must decode separably: 4 = (product of
   // the leading modes) x (a divisor of the next mode's extent)
   bool sep = false;
