@@ -339,7 +339,17 @@ __global__ void __launch_bounds__(NT, 2) tropical_fast_kernel(FastArgs g) {
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r0 = row_of(warp, lane, 0), c0 = col_of(warp, lane, 0);
-  const int64_t G = gridDim.x, c = blockIdx.x;
+  // Work range of this CTA.  Value only: the two CTAs an SM holds (blocks b
+  // and b + G/2 when the grid is two per SM) take neighbouring ranges, which
+  // measured 2.4 % faster (their tiles overlap).  With argmax they keep
+  // ranges G/2 apart, in the same phase of the tile: their resolve passes
+  // coincide, so neither competes with the other's main loop for the
+  // shared-memory pipe (measured 1.8 % faster than out of phase).
+  const int64_t G = gridDim.x;
+  const int64_t c = (!ARGMAX && G % 2 == 0)
+                        ? (blockIdx.x < G / 2 ? 2 * (int64_t)blockIdx.x
+                                              : 2 * ((int64_t)blockIdx.x - G / 2) + 1)
+                        : (int64_t)blockIdx.x;
   const int64_t W = (int64_t)g.tiles * g.T;
   const int64_t u0 = unit_begin(c, W, G), u1 = unit_begin(c + 1, W, G);
   uint32_t* masks = g.ws + (size_t)c * g.max_units * NT;
