@@ -639,7 +639,11 @@ __global__ void special_scan_kernel(ScanArgs s0, ScanArgs s1, uint32_t* flags) {
   for (int w = 0; w < 2; ++w) {
     const ScanArgs& s = w ? s1 : s0;
     const int64_t vec = s.inner / 4, total = vec * s.lines;
+    // a dense operand (lines back to back, batches back to back) is one run:
+    // no index arithmetic per vector
+    const bool flat = s.ld == s.inner && (s.lines <= s.outer || s.bs == (int64_t)s.inner * s.outer);
     auto at = [&](int64_t i) {
+      if (flat) return ((const float4*)s.p)[i];
       const int64_t l = i / vec, v = i - l * vec;
       return ((const float4*)(s.p + (l % s.outer) * s.ld + (l / s.outer) * s.bs))[v];
     };
