@@ -108,10 +108,12 @@ struct SpNode {
   const void* xa;  // binary: left child's values; unary: the input's values
   const void* xb;  // binary: right child's values
   int64_t aux;     // unary: first word of its descriptor in the aux array
+  int64_t kext;    // binary: number of contracted index values
 };
 struct SpMode {
   int64_t ext, sa, sb;  // extent; element stride in the left / right child (0 if absent)
   int64_t da, db;       // the same in the children's memory (their value strides)
+  FastDiv fd;           // division by ext (extents below 2^32)
 };
 
 template <typename T>
@@ -171,6 +173,10 @@ __global__ void __launch_bounds__(512) sparse_backward_kernel(const SpNode* __re
 // Unary descriptor words in aux: nx, ny, ninner, nslots, xslot[nx],
 // xstride[nx], xlogical[nx], yslot[ny], ysize[ny], islot[ninner],
 // isize[ninner].
+// binary entries with more contracted index values than this take the whole
+// block instead of one warp
+constexpr int64_t kLazyBlockK = 4096;
+
 template <typename T, int ALG>
 __device__ __forceinline__ void lazy_better(T v, int64_t k, T& best, int64_t& bk) {
   if (Semi<ALG, T>::better(v, best) || (v == best && k < bk)) {
@@ -186,6 +192,9 @@ __global__ void __launch_bounds__(1024) sparse_backward_lazy_kernel(
     int64_t* lists, const T* __restrict__ val, int64_t n) {
   using S = Semi<ALG, T>;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  __shared__ T bbest[32];
+  __shared__ int64_t bkk[32];
+  __shared__ bool bnan[32];
   for (int64_t e = threadIdx.x; e < n; e += blockDim.x) lists[(int64_t)root * n + e] = e;
   __syncthreads();
   for (int L = 0; L < nlevels; ++L) {
@@ -263,6 +272,8 @@ __global__ void __launch_bounds__(1024) sparse_backward_lazy_kernel(
         }
         first_nan = __shfl_sync(0xffffffffu, first_nan, 0);
         if (lane == 0) lists[(int64_t)nd.child0 * n + e] = (skip || first_nan || bk == INT64_MAX) ? 0 : bpos;
+      } else if (nd.lazy && !nd.argmax && nd.kext > kLazyBlockK) {
+        continue;  // a long contracted range: the whole block takes it below
       } else {
         const SpMode* m = modes + nd.off;
         int64_t pa = 0, pb = 0, qa = 0, qb = 0, rem = o;
@@ -284,9 +295,11 @@ __global__ void __launch_bounds__(1024) sparse_backward_lazy_kernel(
           const T* B = (const T*)nd.xb;
           auto prod = [&](int64_t kk) {
             int64_t ra = qa, rb = qb;
+            uint32_t r = (uint32_t)kk;  // contracted ranges stay below 2^32
             for (int k = nd.nc; k < nd.nc + nd.nk; ++k) {
-              const int64_t c = kk % m[k].ext;
-              kk /= m[k].ext;
+              const uint32_t q = fast_div(r, m[k].fd);
+              const int64_t c = (int64_t)(r - q * m[k].fd.d);
+              r = q;
               ra += c * m[k].da;
               rb += c * m[k].db;
             }
@@ -338,6 +351,90 @@ __global__ void __launch_bounds__(1024) sparse_backward_lazy_kernel(
       }
     }
     __syncthreads();
+    // entries of binary nodes with a long contracted range: one at a time,
+    // the k range split over the whole block, merged as above
+    for (int64_t it = 0; it < items; ++it) {
+      const int id = first + (int)(it / n);
+      const SpNode nd = nodes[id];
+      if (!(nd.kind == 2 && nd.lazy && !nd.argmax && nd.kext > kLazyBlockK)) continue;
+      const int64_t e = it % n;
+      const int64_t o = lists[(int64_t)id * n + e];
+      const SpMode* m = modes + nd.off;
+      int64_t pa = 0, pb = 0, qa = 0, qb = 0, rem = o;
+      for (int k = 0; k < nd.nc; ++k) {
+        const int64_t c = rem % m[k].ext;
+        rem /= m[k].ext;
+        pa += c * m[k].sa;
+        pb += c * m[k].sb;
+        qa += c * m[k].da;
+        qb += c * m[k].db;
+      }
+      const T* A = (const T*)nd.xa;
+      const T* B = (const T*)nd.xb;
+      auto prod = [&](int64_t kk) {
+        int64_t ra = qa, rb = qb;
+        uint32_t r = (uint32_t)kk;
+        for (int k = nd.nc; k < nd.nc + nd.nk; ++k) {
+          const uint32_t q = fast_div(r, m[k].fd);
+          const int64_t c = (int64_t)(r - q * m[k].fd.d);
+          r = q;
+          ra += c * m[k].da;
+          rb += c * m[k].db;
+        }
+        return S::mul(A[ra], B[rb]);
+      };
+      T best = S::zero();
+      int64_t bk = INT64_MAX;
+      bool nan = false;
+      for (int64_t kk = threadIdx.x; kk < nd.kext; kk += blockDim.x) {
+        const T p = prod(kk);
+        nan |= p != p;
+        if (S::better(p, best)) {
+          best = p;
+          bk = kk;
+        }
+      }
+      for (int sh = 16; sh; sh >>= 1) {
+        const T ob = __shfl_xor_sync(0xffffffffu, best, sh);
+        const int64_t ok = __shfl_xor_sync(0xffffffffu, bk, sh);
+        lazy_better<T, ALG>(ob, ok, best, bk);
+      }
+      nan = __any_sync(0xffffffffu, nan);
+      if (lane == 0) {
+        bbest[warp] = best;
+        bkk[warp] = bk;
+        bnan[warp] = nan;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        bool any_nan = false;
+        for (int q = 0; q < nwarps; ++q) {
+          if (q) lazy_better<T, ALG>(bbest[q], bkk[q], best, bk);
+          any_nan |= bnan[q];
+        }
+        int64_t w = bk == INT64_MAX ? 0 : bk;
+        if (any_nan) {  // the sequential rule, as in the forward
+          T acc = S::zero();
+          w = 0;
+          for (int64_t kk = 0; kk < nd.kext; ++kk) {
+            const T p = prod(kk);
+            if (!S::keep(acc, p)) {
+              acc = p;
+              w = kk;
+            }
+          }
+        }
+        for (int k = nd.nc; k < nd.nc + nd.nk; ++k) {
+          const int64_t c = w % m[k].ext;
+          w /= m[k].ext;
+          pa += c * m[k].sa;
+          pb += c * m[k].sb;
+        }
+        lists[(int64_t)nd.child0 * n + e] = pa;
+        lists[(int64_t)nd.child1 * n + e] = pb;
+      }
+      __syncthreads();
+    }
   }
 }
 
@@ -666,8 +763,9 @@ int Engine::backprop_sparse_linked(const void* dy, const std::vector<const Engin
       for (size_t k = 0; k < t.out_ix.size(); ++k)
         modes.push_back({c.shape[k], stride_in(t.left_ix, l.shape, t.out_ix[k]),
                          stride_in(t.right_ix, rr.shape, t.out_ix[k]), data_in(l, t.out_ix[k]),
-                         data_in(rr, t.out_ix[k])});
+                         data_in(rr, t.out_ix[k]), make_fastdiv((uint32_t)c.shape[k])});
       r.nc = (int)t.out_ix.size();
+      r.kext = 1;
       // contracted labels in left_ix order: the argmax's column-major digits
       for (size_t k = 0; k < t.left_ix.size(); ++k) {
         const int32_t lab = t.left_ix[k];
@@ -675,14 +773,19 @@ int Engine::backprop_sparse_linked(const void* dy, const std::vector<const Engin
         const bool in_c = std::find(t.out_ix.begin(), t.out_ix.end(), lab) != t.out_ix.end();
         if (in_r && !in_c) {
           modes.push_back({l.shape[k], stride_in(t.left_ix, l.shape, lab),
-                           stride_in(t.right_ix, rr.shape, lab), data_in(l, lab), data_in(rr, lab)});
+                           stride_in(t.right_ix, rr.shape, lab), data_in(l, lab), data_in(rr, lab),
+                           make_fastdiv((uint32_t)l.shape[k])});
           r.nk++;
+          r.kext *= l.shape[k];
         }
       }
     }
     recs[q] = r;
   }
   int rc;
+  for (const SpNode& r : recs)
+    if (r.lazy && r.kind == 2 && r.kext >= (int64_t(1) << 32))
+      return set_error(OM_ERR_UNSUPPORTED, "values-only backward: a contracted range of 2^32 or more");
   const size_t b_nodes = sizeof(SpNode) * recs.size(), b_modes = sizeof(SpMode) * modes.size();
   const size_t b_aux = 8 * aux.size();
   const size_t b_levels = sizeof(int) * level_start.size(), b_lists = 8 * order.size() * (size_t)n;

@@ -281,18 +281,28 @@ class Einsum:
         _check(_bind().om_b200_einsum_backward(tape, d.ptr, ptrs))
 
     @staticmethod
-    def backward_tape_linked(tape, d: Storage, grads, links):
-        """links: [(leaf index of `tape`, tape of the contraction that made
-        that leaf, grads of that contraction's inputs)]; one launch walks all
-        tapes (tropical, small output only; raises OmError otherwise)."""
+    def linked_args(tape, d: Storage, grads, links):
+        """The ctypes arguments of om_b200_einsum_backward_linked (see
+        backward_tape_linked); a caller repeating the same backward keeps
+        them and passes them to backward_linked_prepared."""
         P = ctypes.c_void_p
         ptrs = (P * len(grads))(*[g.ptr for g in grads])
         leaf = _i32([l[0] for l in links])
         tapes = (P * len(links))(*[l[1] for l in links])
         rows = [(P * len(l[2]))(*[g.ptr for g in l[2]]) for l in links]
         rowp = (P * len(links))(*[ctypes.cast(r, P) for r in rows])
-        _check(_bind().om_b200_einsum_backward_linked(tape, d.ptr, ptrs, len(links), _p(leaf),
-                                                      tapes, rowp))
+        return (tape, d.ptr, ptrs, len(links), _p(leaf), tapes, rowp, leaf, rows)
+
+    @staticmethod
+    def backward_linked_prepared(args):
+        _check(_bind().om_b200_einsum_backward_linked(*args[:7]))
+
+    @staticmethod
+    def backward_tape_linked(tape, d: Storage, grads, links):
+        """links: [(leaf index of `tape`, tape of the contraction that made
+        that leaf, grads of that contraction's inputs)]; one launch walks all
+        tapes (tropical, small output only; raises OmError otherwise)."""
+        Einsum.backward_linked_prepared(Einsum.linked_args(tape, d, grads, links))
 
     @staticmethod
     def tape_free(tape):

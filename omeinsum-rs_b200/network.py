@@ -673,10 +673,12 @@ class DeviceExecutor:
         if plan["dy_val"] != dy:
             self.be.upload_into(plan["dy"], np.asarray([dy], self.dtype))
             plan["dy_val"] = dy
-        leaves = self._reduce(key)[0]
-        links = [(j, lf[3], sg) for j, (lf, sg) in enumerate(zip(leaves, sub_grads))
-                 if lf[0] == "hoisted"]
-        self.E.Einsum.backward_tape_linked(plan["tape"], plan["dy"], grads, links)
+        if "linked" not in plan:  # the same tapes and buffers every time
+            leaves = self._reduce(key)[0]
+            links = [(j, lf[3], sg) for j, (lf, sg) in enumerate(zip(leaves, sub_grads))
+                     if lf[0] == "hoisted"]
+            plan["linked"] = self.E.Einsum.linked_args(plan["tape"], plan["dy"], grads, links)
+        self.E.Einsum.backward_linked_prepared(plan["linked"])
         idx = self.place_index(layout, assign)
         om._check(L.om_b200_scatter_index(self.be.h, dt, gbuf.ptr, len(idx), idx.ptr, dst_ptr, 0))
         if "zero_idx" not in self.__dict__:

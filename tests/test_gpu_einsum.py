@@ -195,3 +195,28 @@ def test_values_only_tape_mis(env, n, seed):
     np.testing.assert_array_equal(c1, c2)
     for x, y in zip(g1, g2):
         np.testing.assert_array_equal(x, y)
+
+
+@pytest.mark.parametrize("kind", ["ties", "specials", "normal"])
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul"])
+def test_values_only_tape_long_contraction(env, alg, kind):
+    # a node contracting 2^14 index values (the block-wide recomputation)
+    om, E, be = env
+    rng = np.random.default_rng(14)
+    lab = list(range(14))
+    ixs = [lab + [14], lab, [14]]
+    iy = []
+    sizes = {l: 2 for l in range(15)}
+    ts = []
+    for ix in ixs:
+        n = 2 ** len(ix)
+        x = (rng.integers(-3, 4, n) if kind != "normal" else rng.standard_normal(n)).astype(np.float32)
+        if kind == "specials":
+            pick = rng.random(n)
+            x[pick < 0.001] = np.nan
+            x[(pick >= 0.001) & (pick < 0.01)] = -np.inf
+        ts.append(x)
+    (c1, g1), (c2, g2) = both_tapes(E, be, alg, ixs, iy, sizes, ts, [1.0], tree=((0, 1), 2))
+    np.testing.assert_array_equal(c1.view(np.uint32), c2.view(np.uint32))
+    for x, y in zip(g1, g2):
+        np.testing.assert_array_equal(x, y)
