@@ -176,6 +176,7 @@ __global__ void __launch_bounds__(512) sparse_backward_kernel(const SpNode* __re
 // binary entries with more contracted index values than this take the whole
 // block instead of one warp
 constexpr int64_t kLazyBlockK = 4096;
+constexpr int kLazyBigQueue = 256;  // such entries per level held in shared memory
 
 template <typename T, int ALG>
 __device__ __forceinline__ void lazy_better(T v, int64_t k, T& best, int64_t& bk) {
@@ -195,11 +196,18 @@ __global__ void __launch_bounds__(1024) sparse_backward_lazy_kernel(
   __shared__ T bbest[32];
   __shared__ int64_t bkk[32];
   __shared__ bool bnan[32];
+  __shared__ int64_t big[kLazyBigQueue];
+  __shared__ int nbig, big_overflow;
   for (int64_t e = threadIdx.x; e < n; e += blockDim.x) lists[(int64_t)root * n + e] = e;
   __syncthreads();
   for (int L = 0; L < nlevels; ++L) {
     const int first = level_start[L];
     const int64_t items = (int64_t)(level_start[L + 1] - first) * n;
+    if (threadIdx.x == 0) {
+      nbig = 0;
+      big_overflow = 0;
+    }
+    __syncthreads();
     for (int64_t it = warp; it < items; it += nwarps) {
       const int id = first + (int)(it / n);
       const int64_t e = it % n;
@@ -273,7 +281,13 @@ __global__ void __launch_bounds__(1024) sparse_backward_lazy_kernel(
         first_nan = __shfl_sync(0xffffffffu, first_nan, 0);
         if (lane == 0) lists[(int64_t)nd.child0 * n + e] = (skip || first_nan || bk == INT64_MAX) ? 0 : bpos;
       } else if (nd.lazy && !nd.argmax && nd.kext > kLazyBlockK) {
-        continue;  // a long contracted range: the whole block takes it below
+        // a long contracted range: queued for the whole block below
+        if (lane == 0) {
+          const int at = atomicAdd(&nbig, 1);
+          if (at < kLazyBigQueue) big[at] = it;
+          else big_overflow = 1;
+        }
+        continue;
       } else {
         const SpMode* m = modes + nd.off;
         int64_t pa = 0, pb = 0, qa = 0, qb = 0, rem = o;
@@ -352,8 +366,11 @@ __global__ void __launch_bounds__(1024) sparse_backward_lazy_kernel(
     }
     __syncthreads();
     // entries of binary nodes with a long contracted range: one at a time,
-    // the k range split over the whole block, merged as above
-    for (int64_t it = 0; it < items; ++it) {
+    // the k range split over the whole block, merged as above (the queue
+    // filled above; on overflow every entry of the level is looked at)
+    const int nq = big_overflow ? (int)items : min(nbig, kLazyBigQueue);
+    for (int qi = 0; qi < nq; ++qi) {
+      const int64_t it = big_overflow ? qi : big[qi];
       const int id = first + (int)(it / n);
       const SpNode nd = nodes[id];
       if (!(nd.kind == 2 && nd.lazy && !nd.argmax && nd.kext > kLazyBlockK)) continue;
