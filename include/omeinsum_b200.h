@@ -283,6 +283,17 @@ int om_b200_graph_end(om_backend* be, om_graph** graph_out);
 int om_b200_graph_launch(om_backend* be, om_graph* graph);
 int om_b200_graph_free(om_graph* graph);
 
+/* Concurrent branches of a recording (no reference counterpart): after
+ * om_b200_graph_branch(be, b) with 0 <= b < 64, the work issued on the
+ * backend is recorded on branch b, which starts after everything recorded
+ * before the first branch call; om_b200_graph_branch(be, -1) returns to the
+ * backend's own stream.  om_b200_graph_end joins every branch, so the graph
+ * ends after all of them.  Branches run concurrently at replay and must use
+ * disjoint buffers; blocks the library frees inside them are not reused
+ * within the recording.  Tropical f32 GEMMs inside branches take the exact
+ * compare-select path (the fast path's gate word is one per backend). */
+int om_b200_graph_branch(om_backend* be, int branch);
+
 /* Allocation-free tropical matrix product with argmax.  No counterpart in the
  * reference: it exists for callers that must not allocate device memory
  * while they run (a host that hands all device memory out of its own arena,

@@ -40,7 +40,7 @@ EXPORTS = [
     "om_b200_tropical_matmul_argmax_noalloc", "om_b200_einsum", "om_b200_einsum_backward",
     "om_b200_tape_free", "om_b200_graph_begin", "om_b200_graph_end", "om_b200_graph_launch",
     "om_b200_graph_free", "om_b200_tape_release", "om_b200_einsum_backward_linked",
-    "om_b200_set_f32_mode", "om_b200_scatter_index", "om_b200_gather_views", "om_b200_einsum_tape_values", "om_b200_optimize_tree",
+    "om_b200_set_f32_mode", "om_b200_scatter_index", "om_b200_gather_views", "om_b200_einsum_tape_values", "om_b200_optimize_tree", "om_b200_graph_branch",
 ]
 
 
@@ -85,6 +85,7 @@ def lib():
         L.om_b200_tropical_backward.argtypes = [P, I, P, P, I, P, P, I, P, P, I, P, P, P, P]
         L.om_b200_launch_count.restype = I64
         L.om_b200_graph_begin.argtypes = [P]
+        L.om_b200_graph_branch.argtypes = [P, I]
         L.om_b200_graph_end.argtypes = [P, ctypes.POINTER(P)]
         L.om_b200_graph_launch.argtypes = [P, P]
         L.om_b200_graph_free.argtypes = [P]
@@ -240,6 +241,11 @@ class B200:
     def graph_begin(self):
         """Start recording the work issued on this backend's stream."""
         _check(lib().om_b200_graph_begin(self.h))
+
+    def graph_branch(self, branch: int):
+        """While recording: issue the following work on concurrent branch
+        `branch` (-1: back to the backend's own stream)."""
+        _check(lib().om_b200_graph_branch(self.h, branch))
 
     def graph_end(self) -> "Graph":
         """Stop recording; the recorded work as a replayable graph."""

@@ -144,6 +144,10 @@ int Arena::alloc(size_t bytes, void** out) {
 }
 
 void Arena::release(void* p) {
+  if (defer) {
+    deferred.push_back(p);
+    return;
+  }
   auto it = used.find((char*)p);
   if (it == used.end()) return;
   char* a = it->first;
@@ -269,6 +273,10 @@ int om_b200_destroy(om_backend* be) {
   resolve_pending(be);
   cudaFree(be->d_flags);
   be->d_flags = nullptr;
+  for (cudaStream_t st : be->branch_streams) cudaStreamDestroy(st);
+  be->branch_streams.clear();
+  if (be->fork_event) cudaEventDestroy(be->fork_event);
+  be->fork_event = nullptr;
   cudaStreamDestroy(be->stream);
   be->stream = nullptr;
   be->pending.clear();
@@ -383,10 +391,73 @@ extern "C" int om_b200_graph_begin(om_backend* be) {
   return OM_OK;
 }
 
+extern "C" int om_b200_graph_branch(om_backend* be, int branch) {
+  using namespace om;
+  if (!be) return set_error(OM_ERR_INVALID, "om_b200_graph_branch: null backend");
+  if (!be->recording) return set_error(OM_ERR_INVALID, "om_b200_graph_branch: not recording");
+  if (branch < -1 || branch >= 64) return set_error(OM_ERR_INVALID, "om_b200_graph_branch: branch out of range");
+  OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  if (!be->branching) {
+    // fork point: everything recorded so far on the backend's stream
+    be->main_stream = be->stream;
+    if (!be->fork_event)
+      OM_CUDA(cudaEventCreateWithFlags(&be->fork_event, cudaEventDisableTiming), "fork event");
+    OM_CUDA(cudaEventRecord(be->fork_event, be->main_stream), "fork record");
+    be->branching = true;
+    be->branch_joined.assign(be->branch_streams.size(), 0);
+    be->recording->defer = true;
+  }
+  if (branch < 0) {
+    be->stream = be->main_stream;
+    return OM_OK;
+  }
+  while ((int)be->branch_streams.size() <= branch) {
+    cudaStream_t st;
+    OM_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "branch stream");
+    be->branch_streams.push_back(st);
+    be->branch_joined.push_back(0);
+  }
+  cudaStream_t st = be->branch_streams[branch];
+  if (!be->branch_joined[branch]) {
+    OM_CUDA(cudaStreamWaitEvent(st, be->fork_event, 0), "fork wait");
+    be->branch_joined[branch] = 1;
+  }
+  be->stream = st;
+  return OM_OK;
+}
+
+// joins every branch forked into the recording back into the backend's
+// stream and releases the blocks their work freed
+static int join_branches(om_backend* be) {
+  using namespace om;
+  if (!be->branching) return OM_OK;
+  be->stream = be->main_stream;
+  int rc = OM_OK;
+  for (size_t b = 0; b < be->branch_streams.size(); ++b) {
+    if (!be->branch_joined[b]) continue;
+    cudaEvent_t ev;
+    cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(ev, be->branch_streams[b]);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(be->main_stream, ev, 0);
+    if (e != cudaSuccess && rc == OM_OK) rc = check_cuda(e, "branch join");
+    cudaEventDestroy(ev);
+  }
+  be->branching = false;
+  Arena* a = be->recording;
+  a->defer = false;
+  for (void* p : a->deferred) a->release(p);
+  a->deferred.clear();
+  return rc;
+}
+
 extern "C" int om_b200_graph_end(om_backend* be, om_graph** graph_out) {
   using namespace om;
   if (!be || !graph_out) return set_error(OM_ERR_INVALID, "om_b200_graph_end: null argument");
   OM_CUDA(cudaSetDevice(be->device), "cudaSetDevice");
+  if (be->recording) {
+    const int jr = join_branches(be);
+    if (jr != OM_OK) return jr;
+  }
   Arena* arena = be->recording;
   be->recording = nullptr;
   auto drop_arena = [&] {

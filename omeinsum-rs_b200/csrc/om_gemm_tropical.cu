@@ -719,6 +719,9 @@ int launch_gemm_exact(om_backend* be, const GemmArgs& g);
 int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) {
   *handled = false;
   if (g.dtype != OM_F32 || g.alg == OM_STANDARD) return OM_OK;
+  // the gate word is one per backend: concurrent graph branches would share
+  // it, so they take the exact path
+  if (be->branching) return OM_OK;
   if (g.M < 64 || g.N < 64 || g.K < 32) return OM_OK;
   if (g.M > (1 << 30) || g.N > (1 << 30) || g.K > (1 << 30) || g.batch > 65535) return OM_OK;
   bool amc, bkc;

@@ -25,6 +25,13 @@ struct om_backend {
   // from this arena (owned by the graph) instead of the stream-ordered pool
   om::Arena* recording = nullptr;
   cudaStream_t stream = nullptr;
+  // branches of a recording (om_b200_graph_branch): while one is selected,
+  // `stream` is that branch's stream and `main_stream` the backend's own
+  cudaStream_t main_stream = nullptr;
+  std::vector<cudaStream_t> branch_streams;
+  std::vector<char> branch_joined;  // branch forked into the current recording
+  cudaEvent_t fork_event = nullptr;
+  bool branching = false;           // a recording with branches is open
   int num_sms = 148;
   // device flag word used by kernels that pick a path on the device
   // (special-value scan of the fast tropical GEMM); lives for the backend.
@@ -82,6 +89,10 @@ inline om_dtype real_part(om_dtype dt) { return dt == OM_C64 ? OM_F64 : OM_F32; 
 // recorded work runs on one stream, in recording order, so reusing a freed
 // block inside the arena is safe).
 struct Arena {
+  // while branches record concurrently running work, freed blocks are not
+  // handed out again (another branch may still be using them at replay)
+  bool defer = false;
+  std::vector<void*> deferred;
   std::vector<std::pair<char*, size_t>> chunks;
   std::map<char*, size_t> free_blocks;  // address-ordered, coalesced
   std::map<char*, size_t> used;

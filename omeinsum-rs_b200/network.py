@@ -490,22 +490,89 @@ class DeviceExecutor:
         self._std_plans[key] = sp
         return sp
 
+    MAX_STD_LANES = 8
+
+    def _std_lanes(self, assign, layout, nlanes):
+        """Standard algebra over several slices at once: one recorded graph
+        with `nlanes` concurrent branches (om_b200_graph_branch), each with
+        its own staging buffers, tape, gradient buffer and accumulator, each
+        running a slice's forward with tape, the backward through it and the
+        hoisted subtrees' tapes, and the placement of value and gradients
+        into its accumulator.  A network of many small nodes is bound by the
+        latency of its dependent launches; independent slices side by side
+        fill the GPU instead."""
+        key = (frozenset(assign.keys()), nlanes)
+        sl = self.__dict__.setdefault("_std_lane_plans", {}).get(key)
+        if sl is not None:
+            return sl
+        om = sys.modules[type(self.be).__module__]
+        L = om.lib()
+        dt = om.DTYPES[np.dtype(self.dtype)]
+        skey = frozenset(assign.keys())
+        leaves = self._reduce(skey)[0]
+        dy = self.be.from_slice(np.ones(1, self.dtype))
+        zero_idx = self.be.from_slice(np.zeros(1, np.int64))
+        lanes = []
+        for _ in range(nlanes):
+            plan = self._plan(assign)  # its own staging buffers and output
+            self._select(plan, assign)
+            grads, sub_grads, gbuf, inputs_end = self._grad_buffers(plan, skey)
+            lanes.append({"plan": plan, "grads": grads, "sub_grads": sub_grads, "gbuf": gbuf,
+                          "n": inputs_end, "idx": self.be.alloc(inputs_end, np.int64),
+                          "acc": self.be.alloc(1 + layout.total, self.dtype), "tape": None})
+        self.be.graph_begin()
+        try:
+            for i, ln in enumerate(lanes):
+                self.be.graph_branch(i)
+                plan = ln["plan"]
+                self._gather(plan)
+                ln["tape"] = plan["ein"].forward_tape_views(self.be, self.alg, plan["tensors"],
+                                                            plan["views"], plan["out"])
+                plan["ein"].backward_tape(ln["tape"], dy, ln["grads"])
+                for j, (lf, sg) in enumerate(zip(leaves, ln["sub_grads"])):
+                    if lf[0] == "hoisted":
+                        self.E.Einsum.backward_tape(lf[3], ln["grads"][j], sg)
+                om._check(L.om_b200_scatter_index(self.be.h, dt, ln["gbuf"].ptr, ln["n"],
+                                                  ln["idx"].ptr, ln["acc"].ptr, 1))
+                om._check(L.om_b200_scatter_index(self.be.h, dt, plan["out"].ptr, 1,
+                                                  zero_idx.ptr, ln["acc"].ptr, 1))
+            self.be.graph_branch(-1)
+        finally:
+            graph = self.be.graph_end()
+        sl = {"lanes": lanes, "graph": graph, "layout": layout, "dy": dy, "zero_idx": zero_idx,
+              "iota": self.be.from_slice(np.arange(1 + layout.total, dtype=np.int64))}
+        self._std_lane_plans[key] = sl
+        return sl
+
     def std_sum(self, assigns, layout):
         """Standard algebra: the sum over `assigns` of [value, full gradients]
-        on the device (the plan's accumulator, zeroed first)."""
+        on the device, slices run several at a time side by side
+        (_std_lanes); returns the first lane's accumulator, which holds the
+        total."""
         if not assigns:
             return None
-        sp = self._std_plan(assigns[0], layout)
-        if sp["layout"] is not layout:
+        # lanes: the largest count up to MAX_STD_LANES that divides the slices
+        nl = max(d for d in range(1, self.MAX_STD_LANES + 1) if len(assigns) % d == 0)
+        sl = self._std_lanes(assigns[0], layout, nl)
+        if sl["layout"] is not layout:
             raise ValueError("std_sum: one layout per executor and set of sliced labels")
-        plan = self._ensure_plan(assigns[0])
-        self.be.upload_into(sp["acc"], np.zeros(1 + layout.total, self.dtype))
-        for a in assigns:
-            self._prepare(plan, a)
-            idx = self.place_index(layout, a)
-            self.be.copy_device(sp["idx"].ptr, idx.ptr, len(idx) * 8)
-            sp["graph"].launch()
-        return sp["acc"]
+        om = sys.modules[type(self.be).__module__]
+        zeros = np.zeros(1 + layout.total, self.dtype)
+        for ln in sl["lanes"]:
+            self.be.upload_into(ln["acc"], zeros)
+        for c0 in range(0, len(assigns), nl):
+            for ln, a in zip(sl["lanes"], assigns[c0:c0 + nl]):
+                self._prepare(ln["plan"], a)
+                idx = self.place_index(layout, a)
+                self.be.copy_device(ln["idx"].ptr, idx.ptr, len(idx) * 8)
+            sl["graph"].launch()
+        L = om.lib()
+        dt = om.DTYPES[np.dtype(self.dtype)]
+        acc0 = sl["lanes"][0]["acc"]
+        for ln in sl["lanes"][1:]:
+            om._check(L.om_b200_scatter_index(self.be.h, dt, ln["acc"].ptr, 1 + layout.total,
+                                              sl["iota"].ptr, acc0.ptr, 1))
+        return acc0
 
     def _grad_plan(self, assign):
         """The reduced tree of the value plan (same fixed buffers), its
@@ -741,6 +808,13 @@ class DeviceExecutor:
                     self.E.Einsum.tape_free(sp["tape"])
                 except Exception:
                     pass
+        for sl in getattr(self, "_std_lane_plans", {}).values():
+            for ln in sl["lanes"]:
+                if ln.get("tape") is not None:
+                    try:
+                        self.E.Einsum.tape_free(ln["tape"])
+                    except Exception:
+                        pass
         for slots in getattr(self, "_vslots", {}).values():
             for plan in slots:
                 if plan.get("tape") is not None:
