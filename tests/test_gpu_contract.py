@@ -406,3 +406,31 @@ def test_long_k_few_outputs_split_k(be, alg, special, nout):
         b[[17, 2222]] = [np.nan, -np.inf]
     check_case(be, alg, a, sa, col(sa), [0, 1, 2, 3], b, sb, col(sb), [2, 1, 0, 3], [nout], [3],
                argmax=alg != "standard")
+
+
+@pytest.mark.parametrize("alg", ["maxplus", "standard"])
+def test_graph_branches_match_eager(be, alg):
+    """Four contractions recorded on concurrent graph branches
+    (om_b200_graph_branch) give the eager results; tropical ones take the
+    exact path inside branches (bit-exact against the oracle)."""
+    m, k, n = 192, 96, 160
+    ins = [(orc.uniform(300 + 2 * i, m * k), orc.uniform(301 + 2 * i, k * n)) for i in range(4)]
+    dev = [(be.from_slice(a), be.from_slice(b)) for a, b in ins]
+    outs = [(be.alloc(m * n, np.float32), be.alloc(m * n, np.uint32)) for _ in ins]
+    am = alg != "standard"
+    be.graph_begin()
+    for i, ((A, B), (C, AM)) in enumerate(zip(dev, outs)):
+        be.graph_branch(i)
+        be.contract_into(alg, A, [m, k], [1, m], [0, 1], B, [k, n], [1, k], [1, 2], [m, n],
+                         [0, 2], C, AM if am else None)
+    be.graph_branch(-1)
+    g = be.graph_end()
+    for _ in range(2):
+        g.launch()
+        for (a, b), (C, AM) in zip(ins, outs):
+            if am:
+                rc, ram = orc.gemm(alg, a, b, m, k, n, argmax=True)
+                assert bits_equal(C.to_vec(), rc) and np.array_equal(AM.to_vec(), ram)
+            else:
+                ref = a.reshape(k, m).T.astype(np.float64) @ b.reshape(n, k).T.astype(np.float64)
+                np.testing.assert_allclose(C.to_vec().reshape(n, m).T, ref, rtol=0, atol=1e-4)
