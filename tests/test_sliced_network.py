@@ -3,7 +3,6 @@ slice assignment and the combine step, on CPU ranks (gloo, world size 2)
 with the oracle engine as the per-slice executor.  The GPU counterpart
 (DeviceExecutor on the B200) is in test_gpu_sliced_network.py."""
 import os
-import socket
 
 import numpy as np
 import pytest
@@ -40,14 +39,12 @@ def _case(kind):
     return E, N, oe, alg, ixs, iy, sizes, ts, edges, tree, sliced
 
 
-def _worker(rank, world, port, kind, q):
+def _worker(rank, world, init, kind, q):
     import sys
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import torch.distributed as dist
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     E, N, oe, alg, ixs, iy, sizes, ts, edges, tree, sliced = _case(kind)
     ex = N.OracleExecutor(oe, E, alg, ixs, iy, sizes, ts, tree)
     v, g, win = N.run_sliced(ex, alg, ixs, sizes, sliced, rank, world, dist=dist)
@@ -56,21 +53,19 @@ def _worker(rank, world, port, kind, q):
     dist.destroy_process_group()
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def _init_file(tmp_path):
+    """A rendezvous through a fresh file: no TCP port to race for between
+    tests (a port found free can be taken again before the ranks bind it)."""
+    return "file://" + str(tmp_path / "rendezvous")
 
 
 @pytest.mark.parametrize("kind", ["mis", "maxmul", "ising"])
-def test_two_gloo_ranks_match_single_rank_and_unsliced(kind):
+def test_two_gloo_ranks_match_single_rank_and_unsliced(kind, tmp_path):
     E, N, oe, alg, ixs, iy, sizes, ts, edges, tree, sliced = _case(kind)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, kind, q)) for r in range(2)]
+    init = _init_file(tmp_path)
+    procs = [ctx.Process(target=_worker, args=(r, 2, init, kind, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(2)]
@@ -129,7 +124,7 @@ def test_slice_grad_layout_matches_scatter():
         assert np.array_equal(full, ref)
 
 
-def _leaving_worker(rank, world, port, q):
+def _leaving_worker(rank, world, init, q):
     """Rank 1 computes its slices and leaves before the combine; rank 0 must
     get CombineError within the collective's time limit instead of hanging."""
     import sys
@@ -137,9 +132,7 @@ def _leaving_worker(rank, world, port, q):
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import torch.distributed as dist
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     E, N, oe, alg, ixs, iy, sizes, ts, edges, tree, sliced = _case("mis")
     ex = N.OracleExecutor(oe, E, alg, ixs, iy, sizes, ts, tree)
     if rank == 1:
@@ -151,14 +144,16 @@ def _leaving_worker(rank, world, port, q):
         q.put(("no error", time.time() - t0))
     except N.CombineError as e:
         q.put(("CombineError", time.time() - t0, str(e)[:200]))
+    except BaseException as e:  # reported, so a failure says what happened
+        q.put((type(e).__name__, time.time() - t0, str(e)[:200]))
     os._exit(0)
 
 
-def test_rank_leaving_between_slices_gives_combine_error():
+def test_rank_leaving_between_slices_gives_combine_error(tmp_path):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
+    init = _init_file(tmp_path)
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, init, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = q.get(timeout=120)
