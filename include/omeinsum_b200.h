@@ -85,6 +85,12 @@ int om_b200_free(om_backend* be, void* dptr);
  * (traits.rs:20) is download.  Both are stream-ordered; download waits. */
 int om_b200_upload(om_backend* be, void* dst_device, const void* src_host, size_t bytes);
 int om_b200_download(om_backend* be, void* dst_host, const void* src_device, size_t bytes);
+/* om_b200_download without the wait: the copy is queued on the backend's
+ * stream and dst_host must stay valid until om_b200_sync returns (use pinned
+ * host memory for a truly asynchronous copy).  No counterpart in the
+ * reference (Storage::to_vec always waits); a caller that overlaps one
+ * step's copies with another step's contraction on a second backend uses it. */
+int om_b200_download_async(om_backend* be, void* dst_host, const void* src_device, size_t bytes);
 
 /* Backend::copy_strided (traits.rs:71-77): gathers the strided view
  * (shape, strides, offset in elements) of src into the contiguous

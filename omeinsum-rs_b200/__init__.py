@@ -40,7 +40,7 @@ EXPORTS = [
     "om_b200_tropical_matmul_argmax_noalloc", "om_b200_einsum", "om_b200_einsum_backward",
     "om_b200_tape_free", "om_b200_graph_begin", "om_b200_graph_end", "om_b200_graph_launch",
     "om_b200_graph_free", "om_b200_tape_release", "om_b200_einsum_backward_linked",
-    "om_b200_set_f32_mode", "om_b200_scatter_index", "om_b200_gather_views", "om_b200_einsum_tape_values", "om_b200_optimize_tree", "om_b200_graph_branch",
+    "om_b200_set_f32_mode", "om_b200_scatter_index", "om_b200_gather_views", "om_b200_einsum_tape_values", "om_b200_optimize_tree", "om_b200_graph_branch", "om_b200_download_async",
 ]
 
 
@@ -79,6 +79,7 @@ def lib():
         L.om_b200_free.argtypes = [P, P]
         L.om_b200_upload.argtypes = [P, P, P, SZ]
         L.om_b200_download.argtypes = [P, P, P, SZ]
+        L.om_b200_download_async.argtypes = [P, P, P, SZ]
         L.om_b200_copy_strided.argtypes = [P, I, P, I, P, P, I64, P]
         L.om_b200_contract.argtypes = [P, I, I, P, I, P, P, P, P, I, P, P, P, I, P, P, P, P]
         L.om_b200_unary.argtypes = [P, I, I, P, I, P, P, P, I, P, P, P, P]

@@ -360,6 +360,14 @@ int om_b200_upload(om_backend* be, void* dst, const void* src, size_t bytes) {
   return OM_OK;
 }
 
+int om_b200_download_async(om_backend* be, void* dst, const void* src, size_t bytes) {
+  if (!be || (!dst && bytes) || (!src && bytes))
+    return set_error(OM_ERR_INVALID, "om_b200_download_async: null argument");
+  if (!bytes) return OM_OK;
+  OM_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, be->stream), "download");
+  return OM_OK;
+}
+
 int om_b200_download(om_backend* be, void* dst, const void* src, size_t bytes) {
   if (!be || (!dst && bytes) || (!src && bytes))
     return set_error(OM_ERR_INVALID, "om_b200_download: null argument");
