@@ -168,7 +168,8 @@ def run_reference(args, rank, world):
 def run_permuted(be, om, local_rank):
     """'abcd,dcef->abfe', a=b=e=f=64, c=d=32, f32 N(0,1):
     Standard on the tensor cores (3xTF32) and on the CUDA cores (exact f32
-    FMA), and MinPlus; device-timed per om_b200_contract call (kernels per
+    FMA), and MinPlus; plus the same contraction in Standard f64 (the DFMA
+    kernel); device-timed per om_b200_contract call (kernels per
     class from the profiler), each output checked on sampled rows against
     the oracle first (Standard under the f32 rule, MinPlus bit-exact)."""
     import oracle as orc
@@ -180,24 +181,38 @@ def run_permuted(be, om, local_rank):
     C = be.alloc(a_ ** 4, np.float32)
     col = om.col_strides
     flops = 2.0 * 4096 * 4096 * 1024
-    out = {"workload": "abcd,dcef->abfe a=b=e=f=64 c=d=32 f32", "unit": "TFLOP/s (TOP/s)"}
+    out = {"workload": "abcd,dcef->abfe a=b=e=f=64 c=d=32 f32 (and the same in f64)",
+           "unit": "TFLOP/s (TOP/s)"}
     stream = torch.cuda.ExternalStream(be.stream(), device=local_rank)
     rows = np.array([0, 1, 777, 2048, 4095])
     sub = np.ascontiguousarray(ha.reshape(c_ * c_, a_ * a_)[:, rows].T).reshape(-1, order="F")
     ssub = [len(rows), c_, c_]
-    for alg, mode in (("standard", "3xtf32"), ("standard", "exact"), ("minplus", None)):
-        if mode:
+    A64, B64 = be.from_slice(ha.astype(np.float64)), be.from_slice(hb.astype(np.float64))
+    C64 = be.alloc(a_ ** 4, np.float64)
+    for alg, mode in (("standard", "3xtf32"), ("standard", "exact"), ("minplus", None),
+                      ("standard", "f64")):
+        if mode in ("3xtf32", "exact"):
             be.set_f32_mode(mode)
+        f64 = mode == "f64"
+        Ax, Bx, Cx = (A64, B64, C64) if f64 else (A, B, C)
 
         def call():
-            be.contract_into(alg, A, sa, col(sa), [0, 1, 2, 3], B, sb, col(sb), [3, 2, 4, 5],
-                             [a_] * 4, [0, 1, 5, 4], C, None)
+            be.contract_into(alg, Ax, sa, col(sa), [0, 1, 2, 3], Bx, sb, col(sb), [3, 2, 4, 5],
+                             [a_] * 4, [0, 1, 5, 4], Cx, None)
         for _ in range(3):
             call()
         be.synchronize()
         # sampled-row check of this mode's output
-        got = C.to_vec().reshape(a_ * a_, a_ * a_, order="F")[rows, :]
-        if alg == "standard":
+        got = Cx.to_vec().reshape(a_ * a_, a_ * a_, order="F")[rows, :]
+        if f64:
+            r = orc.contract("standard", sub.astype(np.float64), ssub, col(ssub), [100, 2, 3],
+                             hb.astype(np.float64), sb, col(sb), [3, 2, 4, 5],
+                             [len(rows), a_, a_], [100, 5, 4]).reshape(len(rows), -1, order="F")
+            bound = 1e-12 * np.maximum(np.abs(r), np.max(np.abs(r)))
+            err = float(np.max(np.abs(got - r) / bound))
+            check = {"rule": "|x-r| <= 1e-12 max(|r|, ||r||_inf)",
+                     "max_err_over_bound": round(err, 4), "ok": err <= 1.0}
+        elif alg == "standard":
             r = orc.contract("standard", sub.astype(np.float64), ssub, col(ssub), [100, 2, 3],
                              hb.astype(np.float64), sb, col(sb), [3, 2, 4, 5],
                              [len(rows), a_, a_], [100, 5, 4]).reshape(len(rows), -1, order="F")
@@ -638,7 +653,7 @@ def main():
     ap.add_argument("--headline-only", action="store_true",
                     help="only the headline contraction (no config-2 / network objects)")
     ap.add_argument("--case", default="headline", choices=["headline", "config2", "contract", "network", "slices",
-                             "networks", "scaling"],
+                             "networks", "scaling", "f64"],
                     help="profiling cases: config2 = only the config-2 permuted "
                          "contraction; contract = only warmup + steps headline calls; "
                          "network = only the sliced MIS network, with its kernel breakdown; "
@@ -649,6 +664,22 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.case == "f64":  # profiling: Standard f64 config-2 shape, 5 calls
+        om = load_pkg()
+        be = om.B200(local_rank)
+        import oracle as orc
+        a_, c_ = 64, 32
+        sa, sb = [a_, a_, c_, c_], [c_, c_, a_, a_]
+        A = be.from_slice(orc.normal(SEED + 2, a_ ** 2 * c_ ** 2).astype(np.float64))
+        B = be.from_slice(orc.normal(SEED + 3, a_ ** 2 * c_ ** 2).astype(np.float64))
+        C = be.alloc(a_ ** 4, np.float64)
+        for _ in range(5):
+            be.contract_into("standard", A, sa, om.col_strides(sa), [0, 1, 2, 3], B, sb,
+                             om.col_strides(sb), [3, 2, 4, 5], [a_] * 4, [0, 1, 5, 4], C, None)
+        be.synchronize()
+        print(json.dumps({"case": "f64", "calls": 5}), flush=True)
+        be.close()
         return
     if args.case == "config2":
         import torch

@@ -771,6 +771,8 @@ int launch_gemm(om_backend* be, const GemmArgs& g) {
   if (handled) return OM_OK;
   OM_TRY(launch_gemm_tropical_fast(be, g, &handled));
   if (handled) return OM_OK;
+  OM_TRY(launch_gemm_f64(be, g, &handled));
+  if (handled) return OM_OK;
   return launch_gemm_exact(be, g);
 }
 

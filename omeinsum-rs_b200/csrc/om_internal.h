@@ -152,6 +152,9 @@ struct GemmArgs {
   int64_t ma1 = 0, sam2 = 0, nb1 = 0, sbn2 = 0;
 };
 int launch_gemm(om_backend* be, const GemmArgs& g);
+// Standard f64 GEMM on the FP64 pipes; *handled false leaves the shape to
+// the generic kernels
+int launch_gemm_f64(om_backend* be, const GemmArgs& g, bool* handled);
 // Whether launch_gemm gives this Standard f32 problem to the tensor-core
 // kernel (the only kernel that reads a two-level contracted index).
 bool tf32_takes(const om_backend* be, om_algebra alg, om_dtype dt, bool argmax, int64_t M,
