@@ -434,3 +434,30 @@ def test_graph_branches_match_eager(be, alg):
             else:
                 ref = a.reshape(k, m).T.astype(np.float64) @ b.reshape(n, k).T.astype(np.float64)
                 np.testing.assert_allclose(C.to_vec().reshape(n, m).T, ref, rtol=0, atol=1e-4)
+
+
+@pytest.mark.parametrize("amc", [True, False])
+@pytest.mark.parametrize("bkc", [True, False])
+@pytest.mark.parametrize("shape", [(1100, 1200, 40, 1), (700, 900, 33, 2), (1302, 1000, 17, 1)])
+def test_standard_f64_dfma_orientations(be, amc, bkc, shape):
+    """Standard f64 GEMM shapes large enough for the DFMA kernel, every
+    unit-stride orientation of A and B, ragged tiles and a batch, against
+    numpy within 1e-12 of the largest output."""
+    m, n, k, nb = shape
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal(m * k * nb)
+    b = rng.standard_normal(k * n * nb)
+    # A as [m, k, batch] (m fastest) or [k, m, batch]; B as [k, n, batch] or [n, k, batch]
+    sa = [m, k, nb] if amc else [k, m, nb]
+    ma = [0, 1, 9] if amc else [1, 0, 9]
+    sb = [k, n, nb] if bkc else [n, k, nb]
+    mb = [1, 2, 9] if bkc else [2, 1, 9]
+    A, B = be.from_slice(a), be.from_slice(b)
+    c = be.contract("standard", A, sa, col(sa), ma, B, sb, col(sb), mb, [m, n, nb],
+                    [0, 2, 9]).to_vec().reshape(nb, n, m)
+    at = a.reshape(nb, sa[1], sa[0])
+    bt = b.reshape(nb, sb[1], sb[0])
+    Am = np.transpose(at, (0, 2, 1)) if amc else at          # [batch, m, k]
+    Bm = np.transpose(bt, (0, 2, 1)) if bkc else bt          # [batch, k, n]
+    ref = np.einsum("bmk,bkn->bnm", Am, Bm)
+    assert np.max(np.abs(c - ref)) <= 1e-12 * np.max(np.abs(ref))
