@@ -470,6 +470,55 @@ int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Op
     }
   }
 
+  // The fast tropical f32 kernel and the f64 DFMA kernel read k two-level as
+  // well (per 32- / 16-wide slab): a contracted group that does not flatten
+  // in an operand but splits into two runs is decoded there instead of
+  // gathered, the free groups staying flat (C may still go through the
+  // output permutation).  Without argmax the contracted order may be any
+  // that makes that possible.
+  if (!decoded && dt != OM_U32 && !is_complex(dt) &&
+      (flat_stride(A, contr) < 0 || flat_stride(B, contr) < 0) && contr.size() >= 2 &&
+      flat_stride(A, lfree) >= 0 && flat_stride(B, rfree) >= 0 && flat_stride(A, batch) >= 0 &&
+      flat_stride(B, batch) >= 0 && group_size(A, batch) == 1) {
+    std::vector<std::vector<int32_t>> kc{contr};
+    if (!track) {
+      kc.push_back(sorted_by_stride(A, contr));
+      kc.push_back(sorted_by_stride(B, contr));
+    }
+    for (size_t k = 0; k < kc.size() && !decoded; ++k) {
+      Lv ak, bk;
+      if (!level(A, kc[k], ak) || !level(B, kc[k], bk)) continue;
+      GemmArgs t{};
+      t.alg = alg;
+      t.dtype = dt;
+      t.M = group_size(A, lfree);
+      t.N = group_size(B, rfree);
+      t.K = group_size(A, contr);
+      t.batch = 1;
+      t.A = a;
+      t.B = b;
+      t.sam = flat_stride(A, lfree);
+      t.sbn = flat_stride(B, rfree);
+      t.sak = ak.s1;
+      t.ka1 = ak.n1;
+      t.sak2 = ak.s2;
+      t.sbk = bk.s1;
+      t.kb1 = bk.n1;
+      t.sbk2 = bk.s2;
+      t.argmax = argmax;
+      if (!tropical_fast_takes(t) && !f64_dfma_takes(be, t)) continue;
+      contr = kc[k];
+      a_k = ak;
+      b_k = bk;
+      a_row = Lv{0, t.sam, 0};
+      b_row = Lv{0, t.sbn, 0};
+      decoded = true;
+      if (trace_on())
+        fprintf(stderr, "[om trace] gemm decodes two-level k: A %lld, B %lld\n", (long long)ak.n1,
+                (long long)bk.n1);
+    }
+  }
+
   Scratch ga, gb;
   if (!decoded &&
       (flat_stride(A, lfree) < 0 || flat_stride(A, contr) < 0 || flat_stride(A, batch) < 0)) {

@@ -36,6 +36,7 @@ struct F64Args {
   int64_t ldb, sbb;
   double* C;
   int64_t scm, scn, scb;
+  int64_t ka1 = 0, sak2 = 0, kb1 = 0, sbk2 = 0;  // two-level k (0: flat), multiples of DK
 };
 
 template <bool A_MC, bool B_KC>
@@ -52,38 +53,38 @@ struct F64Stager {
         const int k = u / 64, m = 2 * (u % 64);
         const int64_t gm = m0 + m, gk = k0 + k;
         if (gk < g.K && gm + 1 < g.M) {
-          ra[r] = *(const double2*)(Ab + gm + gk * g.lda);
+          ra[r] = *(const double2*)(Ab + gm + kofs(gk, g.lda, g.ka1, g.sak2));
         } else {
           ra[r] = z;
-          if (gk < g.K && gm < g.M) ra[r].x = Ab[gm + gk * g.lda];
+          if (gk < g.K && gm < g.M) ra[r].x = Ab[gm + kofs(gk, g.lda, g.ka1, g.sak2)];
         }
       } else {  // A[m*lda + k]: pairs along k
         const int m = u / 8, k = 2 * (u % 8);
         const int64_t gm = m0 + m, gk = k0 + k;
         if (gm < g.M && gk + 1 < g.K) {
-          ra[r] = *(const double2*)(Ab + gm * g.lda + gk);
+          ra[r] = *(const double2*)(Ab + gm * g.lda + kofs(gk, 1, g.ka1, g.sak2));
         } else {
           ra[r] = z;
-          if (gm < g.M && gk < g.K) ra[r].x = Ab[gm * g.lda + gk];
+          if (gm < g.M && gk < g.K) ra[r].x = Ab[gm * g.lda + kofs(gk, 1, g.ka1, g.sak2)];
         }
       }
       if (B_KC) {  // B[k + n*ldb]: pairs along k
         const int n = u / 8, k = 2 * (u % 8);
         const int64_t gn = n0 + n, gk = k0 + k;
         if (gn < g.N && gk + 1 < g.K) {
-          rb[r] = *(const double2*)(Bb + gn * g.ldb + gk);
+          rb[r] = *(const double2*)(Bb + gn * g.ldb + kofs(gk, 1, g.kb1, g.sbk2));
         } else {
           rb[r] = z;
-          if (gn < g.N && gk < g.K) rb[r].x = Bb[gn * g.ldb + gk];
+          if (gn < g.N && gk < g.K) rb[r].x = Bb[gn * g.ldb + kofs(gk, 1, g.kb1, g.sbk2)];
         }
       } else {  // B[k*ldb + n]: pairs along n
         const int k = u / 64, n = 2 * (u % 64);
         const int64_t gn = n0 + n, gk = k0 + k;
         if (gk < g.K && gn + 1 < g.N) {
-          rb[r] = *(const double2*)(Bb + gn + gk * g.ldb);
+          rb[r] = *(const double2*)(Bb + gn + kofs(gk, g.ldb, g.kb1, g.sbk2));
         } else {
           rb[r] = z;
-          if (gk < g.K && gn < g.N) rb[r].x = Bb[gn + gk * g.ldb];
+          if (gk < g.K && gn < g.N) rb[r].x = Bb[gn + kofs(gk, g.ldb, g.kb1, g.sbk2)];
         }
       }
     }
@@ -195,14 +196,49 @@ int launch_f64(om_backend* be, const F64Args& a) {
 
 }  // namespace
 
-int launch_gemm_f64(om_backend* be, const GemmArgs& g, bool* handled) {
-  *handled = false;
-  if (g.dtype != OM_F64 || g.alg != OM_STANDARD || g.argmax) return OM_OK;
-  if (g.ka1 || g.kb1 || g.ma1 || g.nb1) return OM_OK;
+// orientation of the operands for 16-byte loads, or false
+static bool f64_orient(const GemmArgs& g, bool* amc, int64_t* lda, bool* bkc, int64_t* ldb) {
+  if (g.ma1 || g.nb1) return false;
+  if ((g.ka1 || g.kb1) && g.batch != 1) return false;
+  if (g.ka1 && (g.ka1 % DK || g.sak2 % 2)) return false;
+  if (g.kb1 && (g.kb1 % DK || g.sbk2 % 2)) return false;
+  auto ok16 = [](const void* p, int64_t n_unit, int64_t st) {
+    return ((uintptr_t)p % 16) == 0 && n_unit % 2 == 0 && st % 2 == 0;
+  };
+  if (g.sam == 1 && ok16(g.A, g.M, g.sak) && g.sab % 2 == 0) {
+    *amc = true;
+    *lda = g.sak;
+  } else if (g.sak == 1 && ok16(g.A, g.K, g.sam) && g.sab % 2 == 0) {
+    *amc = false;
+    *lda = g.sam;
+  } else {
+    return false;
+  }
+  if (g.sbk == 1 && ok16(g.B, g.K, g.sbn) && g.sbb % 2 == 0) {
+    *bkc = true;
+    *ldb = g.sbn;
+  } else if (g.sbn == 1 && ok16(g.B, g.N, g.sbk) && g.sbb % 2 == 0) {
+    *bkc = false;
+    *ldb = g.sbk;
+  } else {
+    return false;
+  }
+  return true;
+}
+
+bool f64_dfma_takes(om_backend* be, const GemmArgs& g) {
+  bool amc, bkc;
+  int64_t lda, ldb;
   // large enough for 128 x 128 tiles to pay; smaller shapes keep the
   // generic kernels
-  if (g.M < 64 || g.N < 64 || g.K < 16 || g.M * g.N * g.batch < (int64_t)be->num_sms * DM * DN / 2)
-    return OM_OK;
+  return g.dtype == OM_F64 && g.alg == OM_STANDARD && !g.argmax && g.M >= 64 && g.N >= 64 &&
+         g.K >= 16 && g.M * g.N * g.batch >= (int64_t)be->num_sms * DM * DN / 2 &&
+         f64_orient(g, &amc, &lda, &bkc, &ldb);
+}
+
+int launch_gemm_f64(om_backend* be, const GemmArgs& g, bool* handled) {
+  *handled = false;
+  if (!f64_dfma_takes(be, g)) return OM_OK;
   F64Args a;
   a.M = g.M;
   a.N = g.N;
@@ -216,30 +252,12 @@ int launch_gemm_f64(om_backend* be, const GemmArgs& g, bool* handled) {
   a.scm = g.scm;
   a.scn = g.scn;
   a.scb = g.scb;
+  a.ka1 = g.ka1;
+  a.sak2 = g.sak2;
+  a.kb1 = g.kb1;
+  a.sbk2 = g.sbk2;
   bool amc, bkc;
-  // 16-byte loads want the unit-stride axis even in length and the other
-  // stride even, and the base 16-byte aligned
-  auto ok16 = [](const void* p, int64_t n_unit, int64_t st) {
-    return ((uintptr_t)p % 16) == 0 && n_unit % 2 == 0 && st % 2 == 0;
-  };
-  if (g.sam == 1 && ok16(g.A, g.M, g.sak) && g.sab % 2 == 0) {
-    amc = true;
-    a.lda = g.sak;
-  } else if (g.sak == 1 && ok16(g.A, g.K, g.sam) && g.sab % 2 == 0) {
-    amc = false;
-    a.lda = g.sam;
-  } else {
-    return OM_OK;
-  }
-  if (g.sbk == 1 && ok16(g.B, g.K, g.sbn) && g.sbb % 2 == 0) {
-    bkc = true;
-    a.ldb = g.sbn;
-  } else if (g.sbn == 1 && ok16(g.B, g.N, g.sbk) && g.sbb % 2 == 0) {
-    bkc = false;
-    a.ldb = g.sbk;
-  } else {
-    return OM_OK;
-  }
+  f64_orient(g, &amc, &a.lda, &bkc, &a.ldb);
   *handled = true;
   if (amc && bkc) return launch_f64<true, true>(be, a);
   if (amc) return launch_f64<true, false>(be, a);

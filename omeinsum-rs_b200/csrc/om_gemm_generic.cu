@@ -60,14 +60,14 @@ __global__ void __launch_bounds__(256) gemm_tiled(GemmArgs g) {
         int e = tid + r * 256;
         int mm = e % BM, kk = e / BM;
         int64_t m = m0 + mm, k = k0 + kk;
-        As[kk][mm] = (m < g.M && kk < kc) ? Ab[m * g.sam + k * g.sak] : T(0);
+        As[kk][mm] = (m < g.M && kk < kc) ? Ab[m * g.sam + kofs(k, g.sak, g.ka1, g.sak2)] : T(0);
       }
 #pragma unroll
       for (int r = 0; r < (BN * BK) / 256; ++r) {
         int e = tid + r * 256;
         int kk = e % BK, nn = e / BK;
         int64_t n = n0 + nn, k = k0 + kk;
-        Bs[kk][nn] = (n < g.N && kk < kc) ? Bb[k * g.sbk + n * g.sbn] : T(0);
+        Bs[kk][nn] = (n < g.N && kk < kc) ? Bb[kofs(k, g.sbk, g.kb1, g.sbk2) + n * g.sbn] : T(0);
       }
       __syncthreads();
 #pragma unroll 4
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(256) gemm_small(GemmArgs g, int64_t total, Fas
     T acc = S::zero();
     uint32_t idx = 0;
     for (int64_t k = 0; k < g.K; ++k) {
-      T av = a[k * g.sak], bv = b[k * g.sbk];
+      T av = a[kofs(k, g.sak, g.ka1, g.sak2)], bv = b[kofs(k, g.sbk, g.kb1, g.sbk2)];
       if (ALG == OM_STANDARD) {
         acc = fma(av, bv, acc);
       } else {

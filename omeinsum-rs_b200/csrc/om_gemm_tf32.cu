@@ -401,8 +401,10 @@ bool tf32_takes(const om_backend* be, om_algebra alg, om_dtype dt, bool argmax, 
 int launch_gemm_tf32(om_backend* be, const GemmArgs& g, bool* handled) {
   *handled = false;
   if (!tf32_takes(be, g.alg, g.dtype, g.argmax != nullptr, g.M, g.N, g.K, g.batch)) {
-    if (g.ka1 > 0 || g.kb1 > 0 || g.ma1 > 0 || g.nb1 > 0)
-      return set_error(OM_ERR_INVALID, "gemm: two-level index off the tensor-core path");
+    // two-level rows / columns exist only for this path; two-level k is
+    // also read by the fast tropical, f64 and exact kernels
+    if (g.ma1 > 0 || g.nb1 > 0)
+      return set_error(OM_ERR_INVALID, "gemm: two-level rows or columns off the tensor-core path");
     return OM_OK;
   }
   const int64_t Kp = (g.K + TK - 1) / TK * TK;

@@ -152,6 +152,16 @@ struct GemmArgs {
   int64_t ma1 = 0, sam2 = 0, nb1 = 0, sbn2 = 0;
 };
 int launch_gemm(om_backend* be, const GemmArgs& g);
+// Whether the fast tropical kernel / the f64 DFMA kernel takes these
+// arguments (orientation, alignment, two-level k)
+bool tropical_fast_takes(const GemmArgs& g);
+bool f64_dfma_takes(om_backend* be, const GemmArgs& g);
+#ifdef __CUDACC__
+// offset of contracted index k along a possibly two-level k (n1 == 0: flat)
+__host__ __device__ __forceinline__ int64_t kofs(int64_t k, int64_t s1, int64_t n1, int64_t s2) {
+  return n1 ? (k % n1) * s1 + (k / n1) * s2 : k * s1;
+}
+#endif
 // Standard f64 GEMM on the FP64 pipes; *handled false leaves the shape to
 // the generic kernels
 int launch_gemm_f64(om_backend* be, const GemmArgs& g, bool* handled);

@@ -461,3 +461,20 @@ def test_standard_f64_dfma_orientations(be, amc, bkc, shape):
     Bm = np.transpose(bt, (0, 2, 1)) if bkc else bt          # [batch, k, n]
     ref = np.einsum("bmk,bkn->bnm", Am, Bm)
     assert np.max(np.abs(c - ref)) <= 1e-12 * np.max(np.abs(ref))
+
+
+@pytest.mark.parametrize("alg,dtype,argmax", [("minplus", np.float32, False),
+                                              ("maxplus", np.float32, True),
+                                              ("standard", np.float64, False)])
+def test_two_level_contracted_group(be, alg, dtype, argmax):
+    """A contracted group (c, d) laid out (c, d) in A and (d, c) in B: without
+    argmax the planner reorders it so B flattens and A's k is decoded in two
+    levels inside the fast tropical / f64 DFMA kernel (no gather); with argmax
+    the order is fixed and B is gathered.  Same results either way."""
+    m, c, d, n = 1024, 32, 32, 1280
+    rng = np.random.default_rng(77)
+    sa, sb = [m, c, d], [d, c, n]
+    a = rng.uniform(-1, 1, m * c * d).astype(dtype)
+    b = rng.uniform(-1, 1, d * c * n).astype(dtype)
+    check_case(be, alg, a, sa, col(sa), [0, 1, 2], b, sb, col(sb), [2, 1, 3], [m, n], [0, 3],
+               argmax=argmax)
