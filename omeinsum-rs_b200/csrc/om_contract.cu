@@ -470,8 +470,8 @@ int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Op
     }
   }
 
-  // The fast tropical f32 kernel and the f64 DFMA kernel read k two-level as
-  // well (per 32- / 16-wide slab): a contracted group that does not flatten
+  // The f64 DFMA kernel reads k two-level as well (per 16-wide slab): a
+  // contracted group that does not flatten
   // in an operand but splits into two runs is decoded there instead of
   // gathered, the free groups staying flat (C may still go through the
   // output permutation).  Without argmax the contracted order may be any
@@ -506,7 +506,7 @@ int contract_impl(om_backend* be, om_algebra alg, om_dtype dt, const void* a, Op
       t.kb1 = bk.n1;
       t.sbk2 = bk.s2;
       t.argmax = argmax;
-      if (!tropical_fast_takes(t) && !f64_dfma_takes(be, t)) continue;
+      if (!f64_dfma_takes(be, t)) continue;
       contr = kc[k];
       a_k = ak;
       b_k = bk;

@@ -104,16 +104,7 @@ struct FastArgs {
   float* part_v;                 // [2 per CTA][NE][NT] piece values
   uint32_t* part_k;              // [2 per CTA][NE][NT] piece first winning k
   uint32_t* arrivals;            // [tiles] pieces of a cut tile finished so far
-  // two-level contracted index (0: flat): k = k1 + ka1 * k2 sits at
-  // k1 * (A's k stride) + k2 * sak2, likewise for B; ka1, kb1 are multiples
-  // of the 32-wide slab, so a slab never straddles the two levels
-  int64_t ka1 = 0, sak2 = 0, kb1 = 0, sbk2 = 0;
 };
-
-// offset of slab start k0 (a multiple of 32) along a possibly two-level k
-__device__ __forceinline__ int64_t koff(int64_t k0, int64_t s1, int64_t n1, int64_t s2) {
-  return n1 ? (k0 % n1) * s1 + (k0 / n1) * s2 : k0 * s1;
-}
 
 // float index of element (row, k) in a k-pair slab of width W
 template <int W>
@@ -137,16 +128,12 @@ struct Stager {
         const int q = (r >> 1) * NT + tid;
         const int mq = q % 32, kp = q / 32;
         const int m = m0 + mq * 4, k = k0 + 2 * kp + (r & 1);
-        ra[r] = (m < g.M && k < g.K)
-                    ? *(const float4*)(Ab + m + koff(k0, g.lda, g.ka1, g.sak2) + (int64_t)(k - k0) * g.lda)
-                    : padv;
+        ra[r] = (m < g.M && k < g.K) ? *(const float4*)(Ab + m + (int64_t)k * g.lda) : padv;
       } else {  // A[m*lda + k]: unit = 4 k at one m
         const int u = tid + r * NT;
         const int mm = u % TB_M, kq = u / TB_M;
         const int m = m0 + mm, k = k0 + kq * 4;
-        ra[r] = (m < g.M && k < g.K)
-                    ? *(const float4*)(Ab + (int64_t)m * g.lda + koff(k0, 1, g.ka1, g.sak2) + (k - k0))
-                    : padv;
+        ra[r] = (m < g.M && k < g.K) ? *(const float4*)(Ab + (int64_t)m * g.lda + k) : padv;
       }
     }
 #pragma unroll
@@ -155,15 +142,11 @@ struct Stager {
         const int u = tid + r * NT;
         const int nn = u % TB_N, kq = u / TB_N;
         const int n = n0 + nn, k = k0 + kq * 4;
-        rb[r] = (n < g.N && k < g.K)
-                    ? *(const float4*)(Bb + (int64_t)n * g.ldb + koff(k0, 1, g.kb1, g.sbk2) + (k - k0))
-                    : padv;
+        rb[r] = (n < g.N && k < g.K) ? *(const float4*)(Bb + (int64_t)n * g.ldb + k) : padv;
       } else {  // B[k*ldb + n]: 256 (k-pair, n-quad) units, rows 2p and 2p+1
         const int nq = tid % 16, kp = tid / 16;
         const int n = n0 + nq * 4, k = k0 + 2 * kp + r;
-        rb[r] = (n < g.N && k < g.K)
-                    ? *(const float4*)(Bb + n + koff(k0, g.ldb, g.kb1, g.sbk2) + (int64_t)(k - k0) * g.ldb)
-                    : padv;
+        rb[r] = (n < g.N && k < g.K) ? *(const float4*)(Bb + n + (int64_t)k * g.ldb) : padv;
       }
     }
   }
@@ -239,8 +222,8 @@ struct ResolveStager {
       const int m = A_MC ? 4 * (c % 32) : c / 8;
       const int k = A_MC ? c / 32 : 4 * (c % 8);
       const bool ok = (m0 + m < g.M) && (k0 + k < g.K);
-      const float* src = ok ? (A_MC ? Ab + (m0 + m) + koff(k0, g.lda, g.ka1, g.sak2) + (int64_t)k * g.lda
-                                    : Ab + (int64_t)(m0 + m) * g.lda + koff(k0, 1, g.ka1, g.sak2) + k)
+      const float* src = ok ? (A_MC ? Ab + (m0 + m) + (int64_t)(k0 + k) * g.lda
+                                    : Ab + (int64_t)(m0 + m) * g.lda + (k0 + k))
                             : Ab;
       cp_async16(RA + a_at(m, k), src, ok);
     }
@@ -250,8 +233,8 @@ struct ResolveStager {
       const int n = B_KC ? c / 8 : 4 * (c % 16);
       const int k = B_KC ? 4 * (c % 8) : c / 16;
       const bool ok = (n0 + n < g.N) && (k0 + k < g.K);
-      const float* src = ok ? (B_KC ? Bb + (int64_t)(n0 + n) * g.ldb + koff(k0, 1, g.kb1, g.sbk2) + k
-                                    : Bb + (n0 + n) + koff(k0, g.ldb, g.kb1, g.sbk2) + (int64_t)k * g.ldb)
+      const float* src = ok ? (B_KC ? Bb + (int64_t)(n0 + n) * g.ldb + (k0 + k)
+                                    : Bb + (n0 + n) + (int64_t)(k0 + k) * g.ldb)
                             : Bb;
       cp_async16(RB + b_at(n, k), src, ok);
     }
@@ -733,44 +716,12 @@ int launch_gemm_exact(om_backend* be, const GemmArgs& g);
 // one unit-stride axis per operand with 16-byte aligned vectors).  It then
 // issues: flag reset, special-value scan, fast kernel (skips itself when the
 // scan rules it out) and the exact kernel gated on the opposite condition.
-// Orientation of the operands for the fast kernel (16-byte loads along a
-// unit-stride axis), or false.  A two-level k (ka1 / kb1 set) is accepted
-// with one batch, when its outer stride keeps 16-byte alignment.
-static bool fast_orient(const GemmArgs& g, bool* amc, int64_t* lda, bool* bkc, int64_t* ldb) {
-  if ((g.ka1 || g.kb1) && (g.batch != 1 || g.ma1 || g.nb1)) return false;
-  if (g.ka1 && (g.ka1 % 32 || g.sak2 % 4)) return false;
-  if (g.kb1 && (g.kb1 % 32 || g.sbk2 % 4)) return false;
-  if (g.sam == 1 && g.sak % 4 == 0 && g.M % 4 == 0) {
-    *amc = true;
-    *lda = g.sak;
-  } else if (g.sak == 1 && g.sam % 4 == 0 && g.K % 4 == 0) {
-    *amc = false;
-    *lda = g.sam;
-  } else {
-    return false;
-  }
-  if (g.sbk == 1 && g.sbn % 4 == 0 && g.K % 4 == 0) {
-    *bkc = true;
-    *ldb = g.sbn;
-  } else if (g.sbn == 1 && g.sbk % 4 == 0 && g.N % 4 == 0) {
-    *bkc = false;
-    *ldb = g.sbk;
-  } else {
-    return false;
-  }
-  return true;
-}
-
-bool tropical_fast_takes(const GemmArgs& g) {
-  bool amc, bkc;
-  int64_t lda, ldb;
-  return g.dtype == OM_F32 && g.alg != OM_STANDARD && g.M >= 64 && g.N >= 64 && g.K >= 32 &&
-         fast_orient(g, &amc, &lda, &bkc, &ldb);
-}
-
 int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) {
   *handled = false;
   if (g.dtype != OM_F32 || g.alg == OM_STANDARD) return OM_OK;
+  // flat (affine) k only: decoding a two-level k per slab here measured
+  // 0.6-3 % slower on flat problems, so the planner gathers instead
+  if (g.ka1 || g.kb1 || g.ma1 || g.nb1) return OM_OK;
   // the gate word is one per backend: concurrent graph branches would share
   // it, so they take the exact path
   if (be->branching) return OM_OK;
@@ -778,7 +729,24 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
   if (g.M > (1 << 30) || g.N > (1 << 30) || g.K > (1 << 30) || g.batch > 65535) return OM_OK;
   bool amc, bkc;
   int64_t lda, ldb;
-  if (!fast_orient(g, &amc, &lda, &bkc, &ldb)) return OM_OK;
+  if (g.sam == 1 && g.sak % 4 == 0 && g.M % 4 == 0) {
+    amc = true;
+    lda = g.sak;
+  } else if (g.sak == 1 && g.sam % 4 == 0 && g.K % 4 == 0) {
+    amc = false;
+    lda = g.sam;
+  } else {
+    return OM_OK;
+  }
+  if (g.sbk == 1 && g.sbn % 4 == 0 && g.K % 4 == 0) {
+    bkc = true;
+    ldb = g.sbn;
+  } else if (g.sbn == 1 && g.sbk % 4 == 0 && g.N % 4 == 0) {
+    bkc = false;
+    ldb = g.sbk;
+  } else {
+    return OM_OK;
+  }
   if (!aligned16(g.A) || !aligned16(g.B) || (g.batch > 1 && (g.sab % 4 || g.sbb % 4))) return OM_OK;
 
   // special-value scan
@@ -790,19 +758,6 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
   sa.ld = lda;
   sa.bs = g.sab;
   sa.lines = (int64_t)sa.outer * g.batch;
-  if (g.ka1) {  // two-level k (one batch): lines follow the two k levels
-    if (amc) {  // line k at (k % ka1) * sak + (k / ka1) * sak2
-      sa.outer = (int)g.ka1;
-      sa.bs = g.sak2;
-      sa.lines = g.K;
-    } else {    // runs of ka1 k at m * sam + k2 * sak2
-      sa.inner = (int)g.ka1;
-      sa.outer = (int)(g.K / g.ka1);
-      sa.ld = g.sak2;
-      sa.bs = g.sam;
-      sa.lines = g.M * sa.outer;
-    }
-  }
   sa.pinf_bit = SV_A_PINF;
   sa.ninf_bit = SV_A_NINF;
   sb.p = (const float*)g.B;
@@ -811,19 +766,6 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
   sb.ld = ldb;
   sb.bs = g.sbb;
   sb.lines = (int64_t)sb.outer * g.batch;
-  if (g.kb1) {
-    if (!bkc) {  // line k at (k % kb1) * sbk + (k / kb1) * sbk2
-      sb.outer = (int)g.kb1;
-      sb.bs = g.sbk2;
-      sb.lines = g.K;
-    } else {     // runs of kb1 k at n * sbn + k2 * sbk2
-      sb.inner = (int)g.kb1;
-      sb.outer = (int)(g.K / g.kb1);
-      sb.ld = g.sbk2;
-      sb.bs = g.sbn;
-      sb.lines = g.N * sb.outer;
-    }
-  }
   sb.pinf_bit = SV_B_PINF;
   sb.ninf_bit = SV_B_NINF;
   const int64_t vecs = std::max(sa.lines * (sa.inner / 4), sb.lines * (sb.inner / 4));
@@ -852,10 +794,6 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
   fa.scb = g.scb;
   fa.argmax = g.argmax;
   fa.gate = be->d_flags;
-  fa.ka1 = g.ka1;
-  fa.sak2 = g.sak2;
-  fa.kb1 = g.kb1;
-  fa.sbk2 = g.sbk2;
   fa.gx = (int)((g.M + TB_M - 1) / TB_M);
   fa.gy = (int)((g.N + TB_N - 1) / TB_N);
   fa.tiles = (int)(fa.gx * fa.gy * g.batch);

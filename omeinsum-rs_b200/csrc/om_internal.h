@@ -152,9 +152,8 @@ struct GemmArgs {
   int64_t ma1 = 0, sam2 = 0, nb1 = 0, sbn2 = 0;
 };
 int launch_gemm(om_backend* be, const GemmArgs& g);
-// Whether the fast tropical kernel / the f64 DFMA kernel takes these
-// arguments (orientation, alignment, two-level k)
-bool tropical_fast_takes(const GemmArgs& g);
+// Whether the f64 DFMA kernel takes these arguments (orientation,
+// alignment, two-level k)
 bool f64_dfma_takes(om_backend* be, const GemmArgs& g);
 #ifdef __CUDACC__
 // offset of contracted index k along a possibly two-level k (n1 == 0: flat)

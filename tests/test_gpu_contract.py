@@ -467,10 +467,10 @@ def test_standard_f64_dfma_orientations(be, amc, bkc, shape):
                                               ("maxplus", np.float32, True),
                                               ("standard", np.float64, False)])
 def test_two_level_contracted_group(be, alg, dtype, argmax):
-    """A contracted group (c, d) laid out (c, d) in A and (d, c) in B: without
-    argmax the planner reorders it so B flattens and A's k is decoded in two
-    levels inside the fast tropical / f64 DFMA kernel (no gather); with argmax
-    the order is fixed and B is gathered.  Same results either way."""
+    """A contracted group (c, d) laid out (c, d) in A and (d, c) in B: for
+    Standard f64 the planner reorders it so B flattens and A's k is decoded
+    in two levels inside the DFMA kernel (no gather); the tropical kernels
+    gather B.  Same results either way."""
     m, c, d, n = 1024, 32, 32, 1280
     rng = np.random.default_rng(77)
     sa, sb = [m, c, d], [d, c, n]
