@@ -124,11 +124,14 @@ def test_slice_grad_layout_matches_scatter():
         assert np.array_equal(full, ref)
 
 
-def _leaving_worker(rank, world, init, q):
+def _leaving_worker(rank, world, init, q, dump):
     """Rank 1 computes its slices and leaves before the combine; rank 0 must
     get CombineError within the collective's time limit instead of hanging."""
+    import faulthandler
     import sys
     import time
+    # a stack dump of every thread if this rank is still alive after 60 s
+    faulthandler.dump_traceback_later(60, exit=True, file=open(f"{dump}.{rank}", "w"))
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import torch.distributed as dist
@@ -146,6 +149,9 @@ def _leaving_worker(rank, world, init, q):
         q.put(("CombineError", time.time() - t0, str(e)[:200]))
     except BaseException as e:  # reported, so a failure says what happened
         q.put((type(e).__name__, time.time() - t0, str(e)[:200]))
+    # the queue writes from a feeder thread: flush it before the hard exit
+    q.close()
+    q.join_thread()
     os._exit(0)
 
 
@@ -153,10 +159,18 @@ def test_rank_leaving_between_slices_gives_combine_error(tmp_path):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     init = _init_file(tmp_path)
-    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, init, q)) for r in range(2)]
+    dump = str(tmp_path / "stacks")
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, init, q, dump)) for r in range(2)]
     for p in procs:
         p.start()
-    res = q.get(timeout=120)
+    try:
+        res = q.get(timeout=120)
+    except Exception:
+        stacks = ""
+        for r in range(2):
+            if os.path.exists(f"{dump}.{r}"):
+                stacks += f"--- rank {r}\n" + open(f"{dump}.{r}").read()
+        raise AssertionError("no result from rank 0; stacks:\n" + stacks)
     for p in procs:
         p.join(timeout=60)
     assert res[0] == "CombineError", res
