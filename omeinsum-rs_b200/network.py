@@ -1013,6 +1013,15 @@ def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device
     def split(out):
         return np.split(out[1:], np.cumsum(full_sizes)[:-1])
 
+    import os
+    import time
+    trace = os.environ.get("OM_B200_TRACE") == "1"
+    tmark = [("start", time.perf_counter())]
+
+    def mark(what):
+        if trace:
+            tmark.append((what, time.perf_counter()))
+
     if alg in TROPICAL:
         minimize = TROPICAL[alg]
         best = None
@@ -1024,33 +1033,52 @@ def run_sliced(executor, alg, ixs, sizes, sliced, rank, world, dist=None, device
             vals = executor.values([assigns[s] for s in mine])
         else:
             vals = [executor.value(assigns[s]) for s in mine]
+        mark("values")
         for s, v in zip(mine, vals):
             key = (order_key(v, minimize) << 32) | (0xFFFFFFFF - s)
             if best is None or key > best:
                 best = key
         # int64 MAX on the unsigned key: shift it into signed order first
         signed = (best - (1 << 63)) if best is not None else -(1 << 63)
-        with ctx:
-            key = torch.tensor([signed], dtype=torch.int64, device=device)
-        if multi:
+        spec = None
+        if on_device and best_slot is not None:
+            # the gradient of this rank's best slice, started before the
+            # combine is known: on the winning rank it is the answer, and the
+            # backward overlaps the all-reduce and the wait for other ranks
             with ctx:
-                _collective(dist, lambda **kw: dist.all_reduce(key, op=dist.ReduceOp.MAX, **kw),
-                            timeout_s, "slice-key all-reduce")
+                spec = torch.zeros(1 + layout.total, dtype=tdt, device=device)
+                executor.grad_best_into(assigns[mine[bpos]], best_slot, layout, spec.data_ptr())
+            mark("backward queued")
+        # the key travels on the default stream, independent of the backend's
+        key = torch.tensor([signed], dtype=torch.int64,
+                           device=device if on_device else None)
+        if multi:
+            _collective(dist, lambda **kw: dist.all_reduce(key, op=dist.ReduceOp.MAX, **kw),
+                        timeout_s, "slice-key all-reduce")
         k = int(key.item()) + (1 << 63)
+        mark("key all-reduce")
         win = 0xFFFFFFFF - (k & 0xFFFFFFFF)
         owner = win % world
         if on_device:
             with ctx:  # every device step on the backend's stream
-                buf = torch.zeros(1 + layout.total, dtype=tdt, device=device)
-                if owner == rank:
-                    if best_slot is not None:  # the winner is this rank's best slice
-                        executor.grad_best_into(assigns[win], best_slot, layout, buf.data_ptr())
-                    else:
+                if spec is not None and owner == rank and mine[bpos] == win:
+                    buf = spec
+                else:
+                    buf = spec if spec is not None else torch.zeros(1 + layout.total, dtype=tdt,
+                                                                    device=device)
+                    if owner == rank:
                         executor.grad_into(assigns[win], layout, buf.data_ptr(), accumulate=False)
                 if multi:
                     _collective(dist, lambda **kw: dist.broadcast(buf, src=owner, **kw),
                                 timeout_s, "gradient broadcast")
+                mark("broadcast")
                 out = buf.cpu().numpy()
+            mark("read back")
+            if trace:
+                import sys
+                print("[om trace] run_sliced rank %d: " % rank + ", ".join(
+                    "%s %.3f ms" % (w, (t - tmark[i][1]) * 1e3)
+                    for i, (w, t) in enumerate(tmark[1:])), file=sys.stderr)
             return float(out[0]), split(out), win
         grads = np.zeros(layout.total, dtype=np.float64)
         value = np.zeros(1)
