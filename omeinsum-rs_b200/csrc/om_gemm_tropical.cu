@@ -716,7 +716,41 @@ int launch_gemm_exact(om_backend* be, const GemmArgs& g);
 // one unit-stride axis per operand with 16-byte aligned vectors).  It then
 // issues: flag reset, special-value scan, fast kernel (skips itself when the
 // scan rules it out) and the exact kernel gated on the opposite condition.
+static int launch_fast_impl(om_backend* be, const GemmArgs& g, bool* handled);
+
+// C = A (x) B, or C^T = B^T (x) A^T when A has fewer than 64 rows and B at
+// least 64 columns: the 64-wide side of the 128 x 64 tile then takes the
+// short dimension (values and first-k argmax are the same: the products
+// a (x) b and b (x) a are equal bit for bit).
 int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) {
+  if (g.M < 64 && g.N >= 64) {
+    GemmArgs t = g;
+    t.M = g.N;
+    t.N = g.M;
+    t.A = g.B;
+    t.sam = g.sbn;
+    t.sak = g.sbk;
+    t.sab = g.sbb;
+    t.B = g.A;
+    t.sbn = g.sam;
+    t.sbk = g.sak;
+    t.sbb = g.sab;
+    t.scm = g.scn;
+    t.scn = g.scm;
+    t.ka1 = g.kb1;
+    t.sak2 = g.sbk2;
+    t.kb1 = g.ka1;
+    t.sbk2 = g.sak2;
+    t.ma1 = g.nb1;
+    t.sam2 = g.sbn2;
+    t.nb1 = g.ma1;
+    t.sbn2 = g.sam2;
+    return launch_fast_impl(be, t, handled);
+  }
+  return launch_fast_impl(be, g, handled);
+}
+
+static int launch_fast_impl(om_backend* be, const GemmArgs& g, bool* handled) {
   *handled = false;
   if (g.dtype != OM_F32 || g.alg == OM_STANDARD) return OM_OK;
   // flat (affine) k only: decoding a two-level k per slab here measured
@@ -725,7 +759,9 @@ int launch_gemm_tropical_fast(om_backend* be, const GemmArgs& g, bool* handled) 
   // the gate word is one per backend: concurrent graph branches would share
   // it, so they take the exact path
   if (be->branching) return OM_OK;
-  if (g.M < 64 || g.N < 64 || g.K < 32) return OM_OK;
+  // a short N (down to 16) wastes part of the tile's 64 columns, still far
+  // ahead of the exact kernel on a long k
+  if (g.M < 64 || g.N < 16 || g.K < 32) return OM_OK;
   if (g.M > (1 << 30) || g.N > (1 << 30) || g.K > (1 << 30) || g.batch > 65535) return OM_OK;
   bool amc, bkc;
   int64_t lda, ldb;

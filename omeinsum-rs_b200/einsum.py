@@ -327,6 +327,22 @@ class Einsum:
             _bind().om_b200_tape_free(tape)
         return out, grads
 
+    def record_forward(self, be: B200, alg, tensors, values_only=False):
+        """Records this einsum's forward with tape as a CUDA graph (the
+        network's many small launches then cost one graph launch).  Returns
+        (graph, out, tape): after every graph.launch() the output is in `out`
+        and backward_tape(tape, dy, grads) gives the gradients; the tape and
+        its buffers live as long as the graph (free the tape with tape_free
+        when done).  values_only: a tropical tape without argmax."""
+        out = be.alloc(self.out_size(), tensors[0].dtype)
+        tape = ctypes.c_void_p()
+        be.graph_begin()
+        try:
+            self._call(be, alg, tensors, out, ctypes.byref(tape), values_only=values_only)
+        finally:
+            graph = be.graph_end()
+        return graph, out, tape
+
     def cost_and_gradient(self, be: B200, alg, tensors, dy=None, values_only=False):
         """cost_and_gradient (backward.rs:769-799).  dy defaults to the
         algebra's one() as in the reference (0 for MaxPlus/MinPlus, so pass

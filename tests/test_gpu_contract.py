@@ -478,3 +478,15 @@ def test_two_level_contracted_group(be, alg, dtype, argmax):
     b = rng.uniform(-1, 1, d * c * n).astype(dtype)
     check_case(be, alg, a, sa, col(sa), [0, 1, 2], b, sb, col(sb), [2, 1, 3], [m, n], [0, 3],
                argmax=argmax)
+
+
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "maxmul"])
+@pytest.mark.parametrize("mnk", [(16, 2048, 512), (40, 96, 1000), (300, 20, 257), (8, 512, 64)])
+def test_tropical_short_side_fast_path(be, alg, mnk):
+    """Few rows (the operands swap so the tile's 64-wide side takes them) or
+    a short N (16..63): the fast kernel with padding, bit-exact values and
+    first-k argmax against the oracle, with ties."""
+    m, n, k = mnk
+    a, b = orc.ties(500 + m, m * k), orc.ties(600 + n, k * n)
+    check_case(be, alg, a, [m, k], [1, m], [0, 1], b, [k, n], [1, k], [1, 2], [m, n], [0, 2],
+               argmax=True)
