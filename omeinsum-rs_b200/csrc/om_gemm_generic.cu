@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(256) gemm_small(GemmArgs g, int64_t total, Fas
 // their operand offsets step by that mode's strides and the outputs leave as
 // one 16-byte store), so the per-output index work is a few integer adds.
 // The output is written at its linear index (contiguous, coalesced).
-constexpr int kNodeKTable = 512, kNodeQuads = 1024;
+constexpr int kNodeKTable = 512, kNodeQuads = 1024, kNodeRep = 64;
 
 template <int V, typename T>
 __device__ __forceinline__ void store_v(T* p, const T (&v)[V]) {
@@ -227,11 +227,12 @@ __device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], 
 
 // Blocks per SM for a gemm_node variant: its inner step holds 2 * k * V
 // operand values in registers (k = KT, or the chunk of four of the generic
-// path) besides its state (about 24 registers; 48 for single outputs, which
-// keep 64-bit offsets), which sets the register cap.
+// path) besides its state (about 40 registers with the loop over B's own
+// row modes; 64 for single outputs, which keep 64-bit offsets), which sets
+// the register cap.
 template <typename T, int KT, int V>
 constexpr int node_min_blocks() {
-  constexpr int regs = 2 * (KT == 0 ? 4 : KT) * V * (int)(sizeof(T) / 4) + (V == 1 ? 48 : 24);
+  constexpr int regs = 2 * (KT == 0 ? 4 : KT) * V * (int)(sizeof(T) / 4) + (V == 1 ? 64 : 40);
   constexpr int b = 65536 / (256 * regs);
   return b > 8 ? 8 : (b < 2 ? 2 : b);
 }
@@ -244,7 +245,25 @@ __global__ void __launch_bounds__(256, (node_min_blocks<T, KT, V>())) gemm_node(
   using Off = std::conditional_t<V == 4, int32_t, int64_t>;
   __shared__ Off ka[kNodeKTable], kb[kNodeKTable];
   __shared__ Off la[kNodeQuads], lb[kNodeQuads];
+  __shared__ int64_t rc[kNodeRep];
+  __shared__ Off rb[kNodeRep];
   const int tid = threadIdx.x;
+  const int R = KT > 0 && g.R > 1 ? g.R : 1;
+  if (KT > 0)
+    for (int q0 = tid; q0 < R; q0 += blockDim.x) {
+      uint32_t r = (uint32_t)q0;
+      int64_t oc = 0;
+      Off ob = 0;
+      for (int j = g.nlow; j < g.nlow + g.nrep; ++j) {
+        const uint32_t q = fast_div(r, g.out[j].div);
+        const uint32_t d = r - q * g.out[j].div.d;
+        oc += (int64_t)d * g.out[j].sc;
+        ob += (Off)d * (Off)g.out[j].sb;
+        r = q;
+      }
+      rc[q0] = oc;
+      rb[q0] = ob;
+    }
   const bool ktab = g.K <= kNodeKTable;
   if (ktab)
     for (int k = tid; k < (int)g.K; k += blockDim.x) {
@@ -289,11 +308,13 @@ __global__ void __launch_bounds__(256, (node_min_blocks<T, KT, V>())) gemm_node(
     if (row >= g.rows) break;
     uint32_t r = (uint32_t)row;
     Off ha = 0, hb = 0;
-    for (int j = g.nlow; j < g.nout; ++j) {
+    int64_t hc = 0;
+    for (int j = g.nlow + (KT > 0 ? g.nrep : 0); j < g.nout; ++j) {
       const uint32_t q = fast_div(r, g.out[j].div);
       const uint32_t d = r - q * g.out[j].div.d;
       ha += (Off)d * (Off)g.out[j].sa;
       hb += (Off)d * (Off)g.out[j].sb;
+      hc += (int64_t)d * g.out[j].sc;
       r = q;
     }
     for (int q = q_first; q < Q; q += q_step) {
@@ -307,27 +328,46 @@ __global__ void __launch_bounds__(256, (node_min_blocks<T, KT, V>())) gemm_node(
         idx[i] = 0;
       }
       if constexpr (KT > 0) {
-        // K == KT: every load of the V outputs is issued before any is used
-        T av[KT][V], bv[KT][V];
+        // K == KT: A's values are loaded once and serve the R row
+        // combinations of B's own modes; every load is issued before use
+        T av[KT][V];
 #pragma unroll
-        for (int k = 0; k < KT; ++k) {
-          load_group<V>(a + ka[k], g.ia, g.wa, av[k]);
-          load_group<V>(b + kb[k], g.ib, g.wb, bv[k]);
-        }
+        for (int k = 0; k < KT; ++k) load_group<V>(a + ka[k], g.ia, g.wa, av[k]);
+        for (int rr = 0; rr < R; ++rr) {
+          T bv[KT][V];
+          const T* br = b + (int64_t)rb[rr];
 #pragma unroll
-        for (int k = 0; k < KT; ++k)
+          for (int k = 0; k < KT; ++k) load_group<V>(br + kb[k], g.ib, g.wb, bv[k]);
 #pragma unroll
           for (int i = 0; i < V; ++i) {
-            if (ALG == OM_STANDARD) {
-              acc[i] = fma(av[k][i], bv[k][i], acc[i]);
-            } else {
-              const T p = S::mul(av[k][i], bv[k][i]);
-              if (!S::keep(acc[i], p)) {
-                acc[i] = p;
-                idx[i] = (uint32_t)k;
+            acc[i] = S::zero();
+            idx[i] = 0;
+          }
+#pragma unroll
+          for (int k = 0; k < KT; ++k)
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+              if (ALG == OM_STANDARD) {
+                acc[i] = fma(av[k][i], bv[k][i], acc[i]);
+              } else {
+                const T p = S::mul(av[k][i], bv[k][i]);
+                if (!S::keep(acc[i], p)) {
+                  acc[i] = p;
+                  idx[i] = (uint32_t)k;
+                }
               }
             }
+          const int64_t e = hc + rc[rr] + (int64_t)q * V;
+          store_v<V>(C + e, acc);
+          if (ARGMAX) {
+            if (ALG == OM_STANDARD) {
+#pragma unroll
+              for (int i = 0; i < V; ++i) idx[i] = 0;
+            }
+            store_idx(g.argmax + e, idx);
           }
+        }
+        continue;
       } else if (ktab) {
         // tabulated k in chunks of four: the chunk's loads go out together
         // and a group of V outputs loads as one vector where it can
@@ -386,7 +426,7 @@ __global__ void __launch_bounds__(256, (node_min_blocks<T, KT, V>())) gemm_node(
           }
         }
       }
-      const int64_t e = row * g.P + (int64_t)q * V;
+      const int64_t e = hc + (int64_t)q * V;
       store_v<V>(C + e, acc);
       if (ARGMAX) {
         if (ALG == OM_STANDARD) {
@@ -419,6 +459,12 @@ int launch_node_typed(om_backend* be, const NodeArgs& g, int vec) {
       case 1: with_v(am, std::integral_constant<int, 1>{}); break;
       case 2: with_v(am, std::integral_constant<int, 2>{}); break;
       case 4: with_v(am, std::integral_constant<int, 4>{}); break;
+      case 8:
+        if constexpr (sizeof(T) == 4) {
+          with_v(am, std::integral_constant<int, 8>{});
+          break;
+        }
+        [[fallthrough]];
       default: with_v(am, std::integral_constant<int, 0>{}); break;
     }
   };
@@ -645,6 +691,25 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
   // to 4 * kNodeQuads outputs
   NodeArgs g = g0;
   const size_t es = dtype_size(g.dtype);
+  // the larger operand goes first (A): its values are the ones a thread
+  // keeps across the other operand's own modes.  Every algebra's product
+  // is commutative, and k's order is the contracted modes' order, which the
+  // swap keeps.
+  {
+    auto footprint = [&](bool is_a) {
+      int64_t n = 1;
+      for (int j = 0; j < g.nout; ++j)
+        if ((is_a ? g.out[j].sa : g.out[j].sb) != 0) n *= g.out[j].div.d;
+      for (int j = 0; j < g.nk; ++j)
+        if ((is_a ? g.kmodes[j].sa : g.kmodes[j].sb) != 0) n *= g.kmodes[j].div.d;
+      return n;
+    };
+    if (footprint(false) > footprint(true)) {
+      std::swap(g.A, g.B);
+      for (int j = 0; j < g.nout; ++j) std::swap(g.out[j].sa, g.out[j].sb);
+      for (int j = 0; j < g.nk; ++j) std::swap(g.kmodes[j].sa, g.kmodes[j].sb);
+    }
+  }
   // A tile row spans the leading output modes while their product stays
   // within kNodeQuads * 4; a large mode that would end the row early (a
   // leading 2 x 2 and then an extent of 2^21 leaves rows of four outputs,
@@ -756,6 +821,36 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
   g.P = (int32_t)P;
   g.rows = g.total / P;
   if (g.rows >= (int64_t(1) << 32)) return set_error(OM_ERR_INVALID, "gemm_node: too many rows");
+  // Row order.  C is contiguous in mode order, so each row mode's C stride
+  // is the product of the extents below it.  The row modes that A (the
+  // larger operand) does not carry are decoded first, so that the rows that
+  // read the same part of A run back to back and A is read from DRAM about
+  // once (in C's own order those rows can lie a whole tensor apart, and a
+  // node of 2^28 outputs then read its 2^28-element operand 7 times over).
+  // When k has a compiled length, the leading such modes (up to kNodeRep
+  // combinations) run inside each thread on A values held in registers.
+  g.nrep = 0;
+  g.R = 1;
+  {
+    int64_t sc = 1;
+    for (int j = 0; j < g.nout; ++j) {
+      g.out[j].sc = sc;
+      sc *= g.out[j].div.d;
+    }
+    NodeMode first[kMaxNodeModes], rest[kMaxNodeModes];
+    int nf = 0, nr = 0;
+    for (int j = g.nlow; j < g.nout; ++j) {
+      if (g.out[j].sa == 0) first[nf++] = g.out[j];
+      else rest[nr++] = g.out[j];
+    }
+    for (int j = 0; j < nf; ++j) g.out[g.nlow + j] = first[j];
+    for (int j = 0; j < nr; ++j) g.out[g.nlow + nf + j] = rest[j];
+    const bool kt = g.K == 1 || g.K == 2 || g.K == 4 || (g.K == 8 && g.dtype == OM_F32);
+    if (kt)
+      while (g.nrep < nf && (int64_t)g.R * g.out[g.nlow + g.nrep].div.d <= kNodeRep)
+        g.R *= (int32_t)g.out[g.nlow + g.nrep++].div.d;
+    g.rows /= g.R;
+  }
   if (g.dtype == OM_F32) {
     OM_DISPATCH_ALG(g.alg, ALG, return launch_node_typed<float, ALG>(be, g, vec));
   } else if (g.dtype == OM_F64) {

@@ -202,6 +202,7 @@ constexpr int kMaxNodeModes = 40;
 struct NodeMode {
   FastDiv div;
   int64_t sa, sb;
+  int64_t sc;  // C stride (gemm_node's row modes; set by its launcher)
 };
 struct NodeArgs {
   om_algebra alg;
@@ -219,6 +220,11 @@ struct NodeArgs {
   NodeMode kmodes[kMaxNodeModes];
   int64_t ia[4], ib[4];  // A/B offsets of the outputs inside a group of 4 (set by the launcher)
   int wa, wb;            // 4: ia = {0,1,2,3}; 2: pairs {0,1},{x,x+1}; 0: all 0; 1: other
+  // gemm_node: the first nrep row modes (out[nlow .. nlow + nrep)) are ones
+  // A does not carry; their R combinations run inside a thread, which keeps
+  // its A values in registers across them (set by the launcher)
+  int nrep;
+  int32_t R;
 };
 int launch_gemm_node(om_backend* be, const NodeArgs& g);
 

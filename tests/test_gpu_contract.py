@@ -361,6 +361,54 @@ def test_node_batched_tiny_k(be, alg):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("alg", ["maxplus", "minplus", "standard"])
+@pytest.mark.parametrize("big", ["a", "b"])
+def test_node_rows_reordered_for_reuse(be, alg, big):
+    """A large operand times a small one whose own modes sit above the large
+    operand's in C (the tensor-network slice shape): the node kernel visits
+    its rows with the small operand's modes fastest and writes each row at
+    its place in C; values and argmax against the oracle."""
+    ml, ms, mc = [0, 1, 2, 3], [3, 2, 4, 5], [0, 1, 4, 2, 5]
+    sl, ss = [256, 96, 2, 8], [8, 2, 5, 3]
+    sc = [256, 96, 5, 2, 3]
+    lg = orc.ties(601, int(np.prod(sl)), -4, 4)
+    sm = orc.ties(602, int(np.prod(ss)), -4, 4)
+    if big == "a":
+        check_case(be, alg, lg, sl, col(sl), ml, sm, ss, col(ss), ms, sc, mc,
+                   argmax=alg != "standard")
+    else:
+        check_case(be, alg, sm, ss, col(ss), ms, lg, sl, col(sl), ml, sc, mc,
+                   argmax=alg != "standard")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("alg", ["maxplus", "maxmul", "standard"])
+@pytest.mark.parametrize("k", [1, 2, 4, 8])
+@pytest.mark.parametrize("reps", [(5, 3), (5, 20)])
+@pytest.mark.parametrize("big", ["a", "b"])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_node_register_reuse(be, alg, k, reps, big, dtype):
+    """Short k (a compiled length) and modes of the small operand alone in
+    C's rows: a thread keeps the large operand's values across those rows'
+    combinations (at most 64 of them; the rest stay rows), with the large
+    operand on either side; values and argmax against the oracle."""
+    r4, r5 = reps
+    ml, ms = [0, 1, 2], [2, 4, 5]
+    sl, ss = [256, 48, k], [k, r4, r5]
+    mc, sc = [0, 4, 1, 5], [256, r4, 48, r5]
+    lg = orc.ties(611 + k, int(np.prod(sl)), -4, 4).astype(dtype)
+    sm = orc.ties(612 + k, int(np.prod(ss)), -4, 4).astype(dtype)
+    if alg == "maxmul":
+        lg, sm = np.abs(lg), np.abs(sm)
+    if big == "a":
+        check_case(be, alg, lg, sl, col(sl), ml, sm, ss, col(ss), ms, sc, mc,
+                   argmax=alg != "standard")
+    else:
+        check_case(be, alg, sm, ss, col(ss), ms, lg, sl, col(sl), ml, sc, mc,
+                   argmax=alg != "standard")
+
+
+@pytest.mark.gpu
 def test_graph_replay_of_contractions(be):
     """om_b200_graph_*: contractions recorded once replay on new input data
     with the same results as eager calls (tropical bit-exact)."""
