@@ -182,19 +182,27 @@ __device__ __forceinline__ void store_idx(uint32_t* p, const uint32_t (&v)[4]) {
 __device__ __forceinline__ void store_idx(uint32_t* p, const uint32_t (&v)[1]) { p[0] = v[0]; }
 
 // The V values of a group at p + off[i]: one 16-byte load when they are
-// contiguous (w = 4) and aligned, two 8/16-byte loads for two pairs (w = 2),
-// one load when all four coincide (w = 0, a broadcast operand), else scalar
-// loads.  Alignment is tested per group.
-// The V values of a group at p + off[i]: one 16-byte load when they are
 // contiguous (w = 4), two 8/16-byte loads for two pairs (w = 2), one load
-// when all four coincide (w = 0, a broadcast operand), else scalar loads.
-// The launcher grants w = 4 / 2 only when every group start is aligned.
+// when all four coincide (w = 0, a broadcast operand), two scalar loads
+// when they are x x y y (w = 3) or x y x y (w = 5: the operand lacks one
+// of the group's two modes), else four scalar loads.  The launcher grants
+// w = 4 / 2 only when every group start is aligned.
 template <int V, typename T>
 __device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], int w,
                                            T (&out)[V]) {
   if constexpr (V == 4) {
     if (w == 0) {
       out[0] = out[1] = out[2] = out[3] = p[0];
+      return;
+    }
+    if (w == 3) {
+      out[0] = out[1] = p[0];
+      out[2] = out[3] = p[off[2]];
+      return;
+    }
+    if (w == 5) {
+      out[0] = out[2] = p[0];
+      out[1] = out[3] = p[off[1]];
       return;
     }
     if (w == 4) {
@@ -225,14 +233,15 @@ __device__ __forceinline__ void load_group(const T* p, const int64_t (&off)[4], 
   for (int i = 0; i < V; ++i) out[i] = p[off[i]];
 }
 
-// Blocks per SM for a gemm_node variant: its inner step holds 2 * k * V
-// operand values in registers (k = KT, or the chunk of four of the generic
-// path) besides its state (about 40 registers with the loop over B's own
-// row modes; 64 for single outputs, which keep 64-bit offsets), which sets
-// the register cap.
+// Blocks per SM for a gemm_node variant: it holds k * V values of A and
+// min(k, 4) * V of B in registers (k = KT, or the chunk of four of the
+// generic path) besides its state (about 36 registers with the loop over
+// B's own row modes; 64 for single outputs, which keep 64-bit offsets),
+// which sets the register cap.
 template <typename T, int KT, int V>
 constexpr int node_min_blocks() {
-  constexpr int regs = 2 * (KT == 0 ? 4 : KT) * V * (int)(sizeof(T) / 4) + (V == 1 ? 64 : 40);
+  constexpr int k = KT == 0 ? 4 : KT;
+  constexpr int regs = (k + (k < 4 ? k : 4)) * V * (int)(sizeof(T) / 4) + (V == 1 ? 64 : 36);
   constexpr int b = 65536 / (256 * regs);
   return b > 8 ? 8 : (b < 2 ? 2 : b);
 }
@@ -333,30 +342,34 @@ __global__ void __launch_bounds__(256, (node_min_blocks<T, KT, V>())) gemm_node(
         T av[KT][V];
 #pragma unroll
         for (int k = 0; k < KT; ++k) load_group<V>(a + ka[k], g.ia, g.wa, av[k]);
+        constexpr int KC = KT < 4 ? KT : 4;  // B's values in chunks of k
         for (int rr = 0; rr < R; ++rr) {
-          T bv[KT][V];
           const T* br = b + (int64_t)rb[rr];
-#pragma unroll
-          for (int k = 0; k < KT; ++k) load_group<V>(br + kb[k], g.ib, g.wb, bv[k]);
 #pragma unroll
           for (int i = 0; i < V; ++i) {
             acc[i] = S::zero();
             idx[i] = 0;
           }
 #pragma unroll
-          for (int k = 0; k < KT; ++k)
+          for (int k0 = 0; k0 < KT; k0 += KC) {
+            T bv[KC][V];
 #pragma unroll
-            for (int i = 0; i < V; ++i) {
-              if (ALG == OM_STANDARD) {
-                acc[i] = fma(av[k][i], bv[k][i], acc[i]);
-              } else {
-                const T p = S::mul(av[k][i], bv[k][i]);
-                if (!S::keep(acc[i], p)) {
-                  acc[i] = p;
-                  idx[i] = (uint32_t)k;
+            for (int k = 0; k < KC; ++k) load_group<V>(br + kb[k0 + k], g.ib, g.wb, bv[k]);
+#pragma unroll
+            for (int k = 0; k < KC; ++k)
+#pragma unroll
+              for (int i = 0; i < V; ++i) {
+                if (ALG == OM_STANDARD) {
+                  acc[i] = fma(av[k0 + k][i], bv[k][i], acc[i]);
+                } else {
+                  const T p = S::mul(av[k0 + k][i], bv[k][i]);
+                  if (!S::keep(acc[i], p)) {
+                    acc[i] = p;
+                    idx[i] = (uint32_t)(k0 + k);
+                  }
                 }
               }
-            }
+          }
           const int64_t e = hc + rc[rr] + (int64_t)q * V;
           store_v<V>(C + e, acc);
           if (ARGMAX) {
@@ -782,7 +795,10 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
     if (vec != 4) return 1;
     if (o[1] == 0 && o[2] == 0 && o[3] == 0) return 0;
     if (o[1] == 1 && o[2] == 2 && o[3] == 3) return 4;
-    return (o[1] == 1 && o[3] == o[2] + 1) ? 2 : 1;
+    if (o[1] == 1 && o[3] == o[2] + 1) return 2;
+    if (o[1] == 0 && o[3] == o[2]) return 3;
+    if (o[2] == 0 && o[3] == o[1]) return 5;
+    return 1;
   };
   for (int i = 0; i < 4; ++i) {
     g.ia[i] = g.ib[i] = 0;
@@ -798,7 +814,7 @@ int launch_gemm_node(om_backend* be, const NodeArgs& g0) {
   // a vector width holds only if every group start is aligned to it: the
   // base, the contracted strides and the stride steps between group starts
   auto aligned_to = [&](int w, bool is_a) {
-    if (w < 2) return true;
+    if (w != 2 && w != 4) return true;
     const uintptr_t base = (uintptr_t)(is_a ? g.A : g.B);
     if (base % (w * es)) return false;
     const int64_t* io = is_a ? g.ia : g.ib;

@@ -219,7 +219,7 @@ struct NodeArgs {
   NodeMode out[kMaxNodeModes];
   NodeMode kmodes[kMaxNodeModes];
   int64_t ia[4], ib[4];  // A/B offsets of the outputs inside a group of 4 (set by the launcher)
-  int wa, wb;            // 4: ia = {0,1,2,3}; 2: pairs {0,1},{x,x+1}; 0: all 0; 1: other
+  int wa, wb;  // 4: ia = {0,1,2,3}; 2: {0,1,x,x+1}; 0: all 0; 3: {0,0,x,x}; 5: {0,x,0,x}; 1: other
   // gemm_node: the first nrep row modes (out[nlow .. nlow + nrep)) are ones
   // A does not carry; their R combinations run inside a thread, which keeps
   // its A values in registers across them (set by the launcher)

@@ -409,6 +409,24 @@ def test_node_register_reuse(be, alg, k, reps, big, dtype):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("alg", ["maxplus", "standard"])
+@pytest.mark.parametrize("k", [2, 8])
+@pytest.mark.parametrize("lead", [[0, 6], [6, 0]])
+def test_node_group_load_patterns(be, alg, k, lead):
+    """Groups of four outputs over two extent-2 modes, one of which the small
+    operand lacks: its four values are x x y y or x y x y (two loads)."""
+    ml, ms = [0, 6, 1, 2], [2, 6, 4, 5]
+    sl, ss = [2, 2, 96, k], [k, 2, 3, 5]
+    mc = lead + [4, 1, 5]
+    ext = {0: 2, 6: 2, 1: 96, 4: 3, 5: 5}
+    sc = [ext[m] for m in mc]
+    lg = orc.ties(621 + k, int(np.prod(sl)), -4, 4)
+    sm = orc.ties(622 + k, int(np.prod(ss)), -4, 4)
+    check_case(be, alg, lg, sl, col(sl), ml, sm, ss, col(ss), ms, sc, mc,
+               argmax=alg != "standard")
+
+
+@pytest.mark.gpu
 def test_graph_replay_of_contractions(be):
     """om_b200_graph_*: contractions recorded once replay on new input data
     with the same results as eager calls (tropical bit-exact)."""
