@@ -22,6 +22,14 @@ def test_header_lists_match_package():
     assert sorted(om.EXPORTS) == declared_symbols()
 
 
+def test_integration_binds_every_declared_symbol():
+    """The reference-side FFI declarations shown for a maintainer cover the
+    header exactly: every entry point, and none that does not exist."""
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    bound = sorted(set(re.findall(r"pub fn (om_b200_\w+)\s*\(", text)))
+    assert bound == declared_symbols()
+
+
 def test_library_exports_every_declared_symbol():
     om = load_pkg()
     L = ctypes.CDLL(om.LIB_PATH)
